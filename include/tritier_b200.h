@@ -1,0 +1,232 @@
+/*
+ * tritier_b200.h -- C ABI of the B200 (sm_100a) TriTierCache decode library
+ * (libtritier_b200.so).
+ *
+ * Every pointer argument is a DEVICE pointer (cudaMalloc / torch CUDA tensor
+ * memory) unless stated otherwise.  `stream` is a cudaStream_t passed as
+ * void* (NULL = legacy default stream).  Calls are stream-ordered and do not
+ * synchronise the device unless stated.  Every entry point returns a
+ * tt_status; the message of the last failure on the calling thread is
+ * available from tt_last_error().  No C++ exception crosses this boundary.
+ *
+ * Metadata ("pbs_metadata_dtype"): meta_fp16 = 1 selects IEEE binary16
+ * scale/zero stored as raw uint16 bits, 0 selects float32 -- the two storage
+ * formats of the reference (csrc/include/quantize_k_avx2.h:5-24).
+ *
+ * Each declaration names the reference interface it replaces (paths relative
+ * to the reference project root).
+ */
+#ifndef TRITIER_B200_H
+#define TRITIER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef enum {
+    TT_OK = 0,
+    TT_ERR_INVALID_ARGUMENT = 1, /* reference std::invalid_argument -> ValueError (bindings.cpp:324) */
+    TT_ERR_OUT_OF_RANGE = 2,     /* reference std::out_of_range -> IndexError (bindings.cpp:326) */
+    TT_ERR_OUT_OF_MEMORY = 3,    /* reference std::bad_alloc -> MemoryError (bindings.cpp:328) */
+    TT_ERR_CUDA = 4,             /* CUDA runtime failure -> RuntimeError */
+    TT_ERR_TIMEOUT = 5,          /* a bounded device-side wait gave up -> RuntimeError */
+    TT_ERR_UNSUPPORTED = 6       /* shape outside what the kernels are built for -> ValueError */
+} tt_status;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* tt_last_error(void);
+/* Library version string and the compute capability the kernels target. */
+const char* tt_version(void);
+/* 1 when `p` is device (or managed) memory the kernels can dereference, 0
+ * otherwise.  Lets a binding accept raw integer addresses the way the
+ * reference's get_contiguous_ptr does (bindings.cpp:34-44) and stage host
+ * buffers through the device.  No compute. */
+int tt_pointer_is_device(const void* p);
+
+/* Kernel timing for benchmarks.  While enabled, every kernel launch of the
+ * library is bracketed by CUDA events recorded on its own stream;
+ * tt_profile_collect() waits for them, returns the summed durations per
+ * kernel kind and clears the record.  Off by default; no reference
+ * counterpart. */
+typedef struct {
+    double maintain_ms;   /* k_engine_maintain */
+    double partial_ms;    /* k_attn_partial (the dominant kernel) */
+    double finalize_ms;   /* k_attn_finalize */
+    int maintain_launches, partial_launches, finalize_launches;
+} tt_kernel_times;
+tt_status tt_profile_enable(int on);
+tt_status tt_profile_collect(tt_kernel_times* out);
+
+/* ---------------------------------------------------------------------- */
+/* Stand-alone kernels                                                     */
+/* ---------------------------------------------------------------------- */
+
+/* Fused single-query decode attention over a dense FP32 token set and the
+ * 2-bit packed background store.  Replaces fused_attention_decode_avx2
+ * (csrc/include/fused_attn_avx2.h:4-40; binding bindings.cpp:99-178,
+ * :340-363).  Layouts (row-major):
+ *   Q [num_q_heads, head_dim]; dense_K/V [dense_count, num_kv_heads, head_dim];
+ *   PBS_K_Packed [num_blocks*(k_group_size/16), num_kv_heads, head_dim] int32;
+ *   PBS_K_Scales/Zeroes [num_blocks, num_kv_heads, head_dim];
+ *   PBS_V_Packed [num_blocks*k_group_size, num_kv_heads, ceil(head_dim/16)];
+ *   PBS_V_Scales/Zeroes [num_blocks*k_group_size, num_kv_heads];
+ *   PBS_token_ids [num_blocks*k_group_size] int64, -1 = empty slot (excluded);
+ *   attn_output [num_q_heads, head_dim];
+ *   mean_attn_weights [dense_count + num_blocks*k_group_size] or NULL.
+ * Dense/PBS pointers may be NULL when their count is 0.  Negative counts ->
+ * TT_ERR_INVALID_ARGUMENT (bindings.cpp:120-128).  Scratch comes from a
+ * per-device workspace owned by the library (grown on demand). */
+tt_status tt_fused_attention_decode(
+    const float* Q, const float* dense_K, const float* dense_V, int dense_count,
+    const int32_t* PBS_K_Packed, const void* PBS_K_Scales, const void* PBS_K_Zeroes,
+    const int32_t* PBS_V_Packed, const void* PBS_V_Scales, const void* PBS_V_Zeroes,
+    const int64_t* PBS_token_ids, int num_blocks, int num_q_heads, int num_kv_heads,
+    int head_dim, float* attn_output, float* mean_attn_weights, int k_group_size,
+    int meta_fp16, void* stream);
+
+/* One K block: K [k_group_size, num_heads, head_dim] -> packed
+ * [k_group_size/16, num_heads, head_dim] words, scale/zero [num_heads, head_dim].
+ * Bit-exact with quantize_k_block_avx2 (csrc/include/quantize_k_avx2.h:4-20;
+ * binding bindings.cpp:180-212). */
+tt_status tt_quantize_k_block(const float* K, uint32_t* packed, void* scale, void* zero,
+                              int num_heads, int head_dim, int k_group_size, int meta_fp16,
+                              void* stream);
+
+/* One V chunk: V [chunk_size, num_heads, head_dim] -> packed
+ * [chunk_size, num_heads, ceil(head_dim/16)] words, scale/zero
+ * [chunk_size, num_heads].  Bit-exact with quantize_v_block_avx2
+ * (csrc/include/quantize_v_avx2.h:4-19; binding bindings.cpp:214-246).
+ * head_dim must be a multiple of 16 (the reference reads past the row
+ * otherwise, csrc/cpu/quantize_v_avx2.cpp:91-92). */
+tt_status tt_quantize_v_block(const float* V, int32_t* packed, void* scale, void* zero,
+                              int num_heads, int head_dim, int chunk_size, int meta_fp16,
+                              void* stream);
+
+/* Replaces dequantize_k_avx2 (csrc/include/dequant_avx2.h:4-21; binding
+ * bindings.cpp:248-281): out [num_blocks*k_group_size, num_heads, head_dim]. */
+tt_status tt_dequantize_k(const int32_t* packed, const void* scale, const void* zero,
+                          float* out, int num_blocks, int num_heads, int head_dim,
+                          int k_group_size, int meta_fp16, void* stream);
+
+/* Replaces dequantize_v_avx2 (csrc/include/dequant_avx2.h:23-38; binding
+ * bindings.cpp:283-315): out [total_tokens, num_heads, head_dim]. */
+tt_status tt_dequantize_v(const int32_t* packed, const void* scale, const void* zero,
+                          float* out, int total_tokens, int num_heads, int head_dim,
+                          int meta_fp16, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Cache engine (device-resident tier state)                              */
+/* ---------------------------------------------------------------------- */
+
+/* Constructor arguments of TriTierCacheEngine (csrc/include/cache_engine.h:81-93;
+ * binding bindings.cpp:385-398).  k_group_size is coerced to 16 unless 32
+ * (cache_engine.cpp:29).  device = CUDA ordinal that owns the state. */
+typedef struct {
+    int num_q_heads;
+    int num_kv_heads;
+    int head_dim;
+    int max_seq_len;
+    int sink_size;
+    int rw_size;
+    float h_ratio;
+    float score_decay;
+    int update_interval;
+    int k_group_size;
+    int meta_fp16;
+    int device;
+} tt_engine_config;
+
+typedef struct tt_engine tt_engine;
+
+/* Counters exposed read-only by the reference binding (bindings.cpp:437-458)
+ * plus the waiting-room fill and the cached threshold. */
+typedef struct {
+    int s_count, rw_count, rw_head_index, hh_count, wr_count;
+    int pbs_allocated_blocks, pbs_blocks_used, pbs_count;
+    int total_processed_tokens, total_evictions, last_calc_pos, max_hh, chunk_size;
+    float cached_threshold;
+} tt_engine_counters;
+
+/* Buffer identifiers for tt_engine_get_buffer (the zero-copy views of
+ * bindings.cpp:461-626, plus the waiting room). */
+typedef enum {
+    TT_BUF_S_K = 0, TT_BUF_S_V, TT_BUF_RW_K, TT_BUF_RW_V, TT_BUF_HH_K, TT_BUF_HH_V,
+    TT_BUF_HH_TOKEN_IDS, TT_BUF_HH_SCORES, TT_BUF_WR_K, TT_BUF_WR_V, TT_BUF_WR_TOKEN_IDS,
+    TT_BUF_PBS_K_PACKED, TT_BUF_PBS_K_SCALES, TT_BUF_PBS_K_ZEROES, TT_BUF_PBS_V_PACKED,
+    TT_BUF_PBS_V_SCALES, TT_BUF_PBS_V_ZEROES, TT_BUF_PBS_TOKEN_IDS, TT_BUF_GLOBAL_ATTN_SCORES,
+    TT_BUF_COUNT
+} tt_buffer_id;
+
+typedef struct {
+    void* data;        /* device pointer */
+    size_t count;      /* elements visible to the reference view */
+    int elem_size;     /* bytes per element */
+    int dtype;         /* 0 float32, 1 int32, 2 int64, 3 uint16 (binary16 bits) */
+} tt_buffer_desc;
+
+/* Replaces TriTierCacheEngine::TriTierCacheEngine (cache_engine.cpp:8-82). */
+tt_status tt_engine_create(const tt_engine_config* cfg, tt_engine** out);
+tt_status tt_engine_destroy(tt_engine* e);
+
+/* Replaces TriTierCacheEngine::step (cache_engine.cpp:397-541; binding
+ * bindings.cpp:399-417): ingest one token (K_new/V_new [num_kv_heads*head_dim]),
+ * evict/route/flush, attend with Q [num_q_heads*head_dim] into attn_output,
+ * decayed score feedback.  Stream-ordered, no host synchronisation. */
+tt_status tt_engine_step(tt_engine* e, const float* Q, const float* K_new, const float* V_new,
+                         float* attn_output, void* stream);
+
+/* One decode step for n independent engines (layers and/or sequences) in one
+ * set of launches.  Q/K_new/V_new/attn_output are host arrays of n device
+ * pointers.  All engines must live on the same device.  No reference
+ * counterpart: the reference is batch-1, one engine per call
+ * (src/tri_tier/integration/patch_model.py:65). */
+tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* const* Q,
+                                 const float* const* K_new, const float* const* V_new,
+                                 float* const* attn_output, void* stream);
+
+/* Replaces TriTierCacheEngine::prefill (cache_engine.cpp:271-395; binding
+ * bindings.cpp:418-436): K_all/V_all [q_len, num_kv_heads, head_dim].
+ * q_len < 0 -> TT_ERR_INVALID_ARGUMENT. */
+tt_status tt_engine_prefill(tt_engine* e, const float* K_all, const float* V_all, int q_len,
+                            void* stream);
+
+/* Reads the device-side counters (synchronises the engine's last stream). */
+tt_status tt_engine_get_counters(tt_engine* e, tt_engine_counters* out);
+
+/* Overwrites the engine's integer state (all fields of `c` except max_hh and
+ * chunk_size), stream-ordered on `stream`.  Together with the writable
+ * buffers of tt_engine_get_buffer this imports a tier layout built elsewhere
+ * (synthetic benchmark states, checkpoints).  The caller keeps the state
+ * consistent (counts within capacity, ids of the packed blocks written).
+ * No reference counterpart: the reference exposes its counters read-only
+ * (bindings.cpp:437-458). */
+tt_status tt_engine_set_counters(tt_engine* e, const tt_engine_counters* c, void* stream);
+
+/* Device pointer and reference-view extent of one tier buffer.  PBS views
+ * are sized by pbs_allocated_blocks (bindings.cpp:545-626); the pointer
+ * stays valid until the engine's PBS storage grows. */
+tt_status tt_engine_get_buffer(tt_engine* e, int which, tt_buffer_desc* out);
+
+/* Replaces TriTierCacheEngine::get_buffer_bytes (cache_engine.cpp:543-568):
+ * the reference's byte formula over its logical buffer sizes. */
+tt_status tt_engine_get_buffer_bytes(tt_engine* e, size_t* out);
+
+/* Bytes this engine actually holds on the device (tiers, PBS capacity,
+ * attention scratch).  No reference counterpart. */
+tt_status tt_engine_device_bytes(tt_engine* e, size_t* out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TRITIER_B200_H */

@@ -1,0 +1,469 @@
+"""Drop-in for the reference extension module ``tri_tier._C`` (csrc/bindings.cpp).
+
+Same callables, argument names, defaults and exception types as
+``bindings.cpp:317-627``, implemented over the C ABI of libtritier_b200.so
+(include/tritier_b200.h).  Every computation runs in the sm_100a kernels; when
+the library or a CUDA device is missing the calls raise.
+
+Argument rules follow ``get_contiguous_ptr`` (bindings.cpp:25-97): an argument
+may be a raw integer address, a tensor exposing ``data_ptr()`` /
+``is_contiguous()``, an object with ``__cuda_array_interface__`` or a
+C-contiguous buffer (numpy).  Device memory is used in place.  Host memory
+(numpy arrays, CPU tensors, host addresses) is staged through device memory:
+inputs are copied in, outputs are copied back before the call returns, so the
+reference's own numpy-based call sites keep working.  Kernels run on the
+current torch CUDA stream of the device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+__all__ = ["fused_attention_decode", "quantize_k_block", "quantize_v_block", "dequantize_k",
+           "dequantize_v", "TriTierCacheEngine", "engine_step_batched"]
+
+_DT_BYTES = {"f32": 4, "i32": 4, "i64": 8, "u16": 2}
+_TORCH_DT = {"f32": torch.float32, "i32": torch.int32, "i64": torch.int64, "u16": torch.int16}
+
+
+def _require_cuda():
+    if not torch.cuda.is_available():
+        raise RuntimeError("tritiercache_b200 needs a CUDA device (B200, sm_100a); no CPU fallback exists.")
+    lib()
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+class _Arg:
+    """Resolved pointer argument: device address plus optional staging."""
+
+    __slots__ = ("ptr", "host_ptr", "stage", "nbytes", "writable")
+
+    def __init__(self):
+        self.ptr = 0
+        self.host_ptr = 0
+        self.stage = None
+        self.nbytes = 0
+        self.writable = False
+
+    def finish(self):
+        if self.stage is not None and self.writable and self.nbytes:
+            host = self.stage.cpu()  # synchronises the stream
+            C.memmove(self.host_ptr, host.data_ptr(), self.nbytes)
+
+
+def _stage_host(addr: int, nbytes: int, writable: bool) -> _Arg:
+    a = _Arg()
+    a.host_ptr, a.nbytes, a.writable = addr, nbytes, writable
+    n = max(nbytes, 1)
+    host = torch.empty(n, dtype=torch.uint8)
+    if nbytes:
+        C.memmove(host.data_ptr(), addr, nbytes)
+    a.stage = host.to("cuda", non_blocking=False)
+    a.ptr = a.stage.data_ptr()
+    return a
+
+
+def _arg(obj, name: str, nbytes: int, writable: bool = False, nullable: bool = False) -> _Arg:
+    a = _Arg()
+    if obj is None:
+        if nullable:
+            return a
+        raise ValueError(f"Argument '{name}' cannot be None.")
+    if isinstance(obj, (int, np.integer)) and not isinstance(obj, bool):
+        addr = int(obj)
+        if addr == 0:
+            if nullable:
+                return a
+            raise ValueError(f"Argument '{name}' pointer address is NULL.")
+        if lib().tt_pointer_is_device(C.c_void_p(addr)):
+            a.ptr = addr
+            return a
+        return _stage_host(addr, nbytes, writable)
+    if hasattr(obj, "data_ptr") and hasattr(obj, "is_contiguous"):
+        if not obj.is_contiguous():
+            raise ValueError(f"Argument '{name}' PyTorch tensor is not contiguous in memory. "
+                             "Call .contiguous() before passing.")
+        addr = int(obj.data_ptr())
+        if addr == 0 and not nullable:
+            raise ValueError(f"Argument '{name}' tensor data pointer is NULL.")
+        if getattr(obj, "is_cuda", False):
+            a.ptr = addr
+            return a
+        return _stage_host(addr, nbytes, writable) if addr else a
+    cai = getattr(obj, "__cuda_array_interface__", None)
+    if cai is not None:
+        if cai.get("strides") not in (None,):
+            shape, strides = cai["shape"], cai["strides"]
+            item = np.dtype(cai["typestr"]).itemsize
+            exp = item
+            for d in range(len(shape) - 1, -1, -1):
+                if shape[d] > 1 and strides[d] != exp:
+                    raise ValueError(f"Argument '{name}' buffer is not C-contiguous in memory.")
+                exp *= shape[d]
+        a.ptr = int(cai["data"][0])
+        if a.ptr == 0 and not nullable:
+            raise ValueError(f"Argument '{name}' buffer data pointer is NULL.")
+        return a
+    try:
+        mv = memoryview(obj)
+    except TypeError:
+        raise ValueError(f"Argument '{name}' has unsupported type '{type(obj)}'. Expected PyTorch tensor, "
+                         "NumPy array, buffer object, or integer memory address.") from None
+    if not mv.c_contiguous:
+        raise ValueError(f"Argument '{name}' buffer is not C-contiguous in memory.")
+    arr = np.asarray(obj)
+    if writable and not arr.flags.writeable:
+        raise ValueError(f"Argument '{name}' buffer is read-only.")
+    addr = arr.__array_interface__["data"][0]
+    if addr == 0:
+        if nullable:
+            return a
+        raise ValueError(f"Argument '{name}' buffer data pointer is NULL.")
+    return _stage_host(addr, min(nbytes, arr.nbytes) if nbytes else arr.nbytes, writable)
+
+
+def _is_fp16(obj, pbs_metadata_dtype: str) -> bool:
+    # bindings.cpp:130-136: the string says "fp16", or the scales' dtype
+    # string contains "float16" / "half".
+    fp16 = pbs_metadata_dtype == "fp16"
+    dt = getattr(obj, "dtype", None)
+    if dt is not None:
+        s = str(dt)
+        if "float16" in s or "half" in s:
+            fp16 = True
+    return fp16
+
+
+def _finish(*args):
+    for a in args:
+        a.finish()
+
+
+def fused_attention_decode(Q_ptr, dense_K_ptr, dense_V_ptr, dense_count, PBS_K_Packed_ptr, PBS_K_Scales_ptr,
+                           PBS_K_Zeroes_ptr, PBS_V_Packed_ptr, PBS_V_Scales_ptr, PBS_V_Zeroes_ptr,
+                           PBS_token_ids_ptr, num_blocks, num_q_heads, num_kv_heads, head_dim, attn_output_ptr,
+                           mean_attn_weights_ptr=None, k_group_size=16, pbs_metadata_dtype="fp32"):
+    """Fused decode attention (bindings.cpp:99-178, :340-363)."""
+    if dense_count < 0:
+        raise ValueError("dense_count must be non-negative.")
+    if num_blocks < 0:
+        raise ValueError("num_blocks must be non-negative.")
+    if num_q_heads <= 0 or num_kv_heads <= 0 or head_dim <= 0:
+        raise ValueError("num_q_heads, num_kv_heads, and head_dim must be positive integers.")
+    _require_cuda()
+    fp16 = _is_fp16(PBS_K_Scales_ptr, pbs_metadata_dtype)
+    mb = 2 if fp16 else 4
+    grp = int(k_group_size)
+    kvs = num_kv_heads * head_dim
+    qhd = (head_dim + 15) // 16
+    ntok = num_blocks * grp
+    z = num_blocks == 0
+    q = _arg(Q_ptr, "Q", num_q_heads * head_dim * 4)
+    dk = _arg(dense_K_ptr, "dense_K", dense_count * kvs * 4, nullable=dense_count == 0)
+    dv = _arg(dense_V_ptr, "dense_V", dense_count * kvs * 4, nullable=dense_count == 0)
+    kp = _arg(PBS_K_Packed_ptr, "PBS_K_Packed", num_blocks * max(grp // 16, 1) * kvs * 4, nullable=z)
+    vp = _arg(PBS_V_Packed_ptr, "PBS_V_Packed", ntok * num_kv_heads * qhd * 4, nullable=z)
+    ids = _arg(PBS_token_ids_ptr, "PBS_token_ids", ntok * 8, nullable=z)
+    out = _arg(attn_output_ptr, "attn_output", num_q_heads * head_dim * 4, writable=True)
+    mw = _arg(mean_attn_weights_ptr, "mean_attn_weights", (dense_count + ntok) * 4, writable=True, nullable=True)
+    ks = _arg(PBS_K_Scales_ptr, "PBS_K_Scales", num_blocks * kvs * mb, nullable=z)
+    kz = _arg(PBS_K_Zeroes_ptr, "PBS_K_Zeroes", num_blocks * kvs * mb, nullable=z)
+    vs = _arg(PBS_V_Scales_ptr, "PBS_V_Scales", ntok * num_kv_heads * mb, nullable=z)
+    vz = _arg(PBS_V_Zeroes_ptr, "PBS_V_Zeroes", ntok * num_kv_heads * mb, nullable=z)
+    st = lib().tt_fused_attention_decode(q.ptr, dk.ptr, dv.ptr, dense_count, kp.ptr, ks.ptr, kz.ptr, vp.ptr,
+                                         vs.ptr, vz.ptr, ids.ptr, num_blocks, num_q_heads, num_kv_heads, head_dim,
+                                         out.ptr, mw.ptr, grp, 1 if fp16 else 0, _stream())
+    check(st, "fused_attention_decode")
+    _finish(out, mw)
+
+
+def quantize_k_block(K, packed, scale, zero, num_heads, head_dim, k_group_size=16, pbs_metadata_dtype="fp32"):
+    """2-bit channel-wise K block quantization (bindings.cpp:180-212)."""
+    _require_cuda()
+    fp16 = _is_fp16(scale, pbs_metadata_dtype)
+    mb = 2 if fp16 else 4
+    n = num_heads * head_dim
+    a_k = _arg(K, "K", k_group_size * n * 4)
+    a_p = _arg(packed, "packed", max(k_group_size // 16, 1) * n * 4, writable=True)
+    a_s = _arg(scale, "scale", n * mb, writable=True)
+    a_z = _arg(zero, "zero", n * mb, writable=True)
+    check(lib().tt_quantize_k_block(a_k.ptr, a_p.ptr, a_s.ptr, a_z.ptr, num_heads, head_dim, k_group_size,
+                                    1 if fp16 else 0, _stream()), "quantize_k_block")
+    _finish(a_p, a_s, a_z)
+
+
+def quantize_v_block(V, packed, scale, zero, num_heads, head_dim, chunk_size=16, pbs_metadata_dtype="fp32"):
+    """2-bit token-wise V quantization (bindings.cpp:214-246)."""
+    _require_cuda()
+    fp16 = _is_fp16(scale, pbs_metadata_dtype)
+    mb = 2 if fp16 else 4
+    qhd = (head_dim + 15) // 16
+    a_v = _arg(V, "V", chunk_size * num_heads * head_dim * 4)
+    a_p = _arg(packed, "packed", chunk_size * num_heads * qhd * 4, writable=True)
+    a_s = _arg(scale, "scale", chunk_size * num_heads * mb, writable=True)
+    a_z = _arg(zero, "zero", chunk_size * num_heads * mb, writable=True)
+    check(lib().tt_quantize_v_block(a_v.ptr, a_p.ptr, a_s.ptr, a_z.ptr, num_heads, head_dim, chunk_size,
+                                    1 if fp16 else 0, _stream()), "quantize_v_block")
+    _finish(a_p, a_s, a_z)
+
+
+def dequantize_k(packed, scale, zero, out, num_blocks, num_heads, head_dim, k_group_size=16,
+                 pbs_metadata_dtype="fp32"):
+    """K dequantization (bindings.cpp:248-281)."""
+    _require_cuda()
+    fp16 = _is_fp16(scale, pbs_metadata_dtype)
+    mb = 2 if fp16 else 4
+    n = num_heads * head_dim
+    a_p = _arg(packed, "packed", num_blocks * max(k_group_size // 16, 1) * n * 4)
+    a_o = _arg(out, "out", num_blocks * k_group_size * n * 4, writable=True)
+    a_s = _arg(scale, "scale", num_blocks * n * mb)
+    a_z = _arg(zero, "zero", num_blocks * n * mb)
+    check(lib().tt_dequantize_k(a_p.ptr, a_s.ptr, a_z.ptr, a_o.ptr, num_blocks, num_heads, head_dim, k_group_size,
+                                1 if fp16 else 0, _stream()), "dequantize_k")
+    _finish(a_o)
+
+
+def dequantize_v(packed, scale, zero, out, total_tokens, num_heads, head_dim, pbs_metadata_dtype="fp32"):
+    """V dequantization (bindings.cpp:283-315)."""
+    _require_cuda()
+    fp16 = _is_fp16(scale, pbs_metadata_dtype)
+    mb = 2 if fp16 else 4
+    qhd = (head_dim + 15) // 16
+    a_p = _arg(packed, "packed", total_tokens * num_heads * qhd * 4)
+    a_o = _arg(out, "out", total_tokens * num_heads * head_dim * 4, writable=True)
+    a_s = _arg(scale, "scale", total_tokens * num_heads * mb)
+    a_z = _arg(zero, "zero", total_tokens * num_heads * mb)
+    check(lib().tt_dequantize_v(a_p.ptr, a_s.ptr, a_z.ptr, a_o.ptr, total_tokens, num_heads, head_dim,
+                                1 if fp16 else 0, _stream()), "dequantize_v")
+    _finish(a_o)
+
+
+class _DeviceView:
+    """__cuda_array_interface__ over engine memory; keeps the engine alive."""
+
+    def __init__(self, ptr: int, shape, typestr: str, owner):
+        self._owner = owner
+        self.__cuda_array_interface__ = {"shape": tuple(int(s) for s in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None,
+                                         "stream": None}
+
+
+_BUF = {"S_K": 0, "S_V": 1, "RW_K": 2, "RW_V": 3, "HH_K": 4, "HH_V": 5, "HH_token_ids": 6, "HH_scores": 7,
+        "WR_K": 8, "WR_V": 9, "WR_token_ids": 10, "PBS_K_Packed": 11, "PBS_K_Scales": 12, "PBS_K_Zeroes": 13,
+        "PBS_V_Packed": 14, "PBS_V_Scales": 15, "PBS_V_Zeroes": 16, "PBS_token_ids": 17,
+        "global_attn_scores": 18}
+_TYPESTR = {0: "<f4", 1: "<i4", 2: "<i8", 3: "<u2"}
+
+
+class TriTierCacheEngine:
+    """Device-resident TriTierCache engine (bindings.cpp:383-627, cache_engine.h:10-123).
+
+    Tier buffers live in GPU memory; ``get_*`` return zero-copy CUDA tensors
+    (the reference returns writable numpy views, bindings.cpp:461-626).  The
+    counter attributes read the device state and therefore wait for the
+    engine's last stream.
+    """
+
+    def __init__(self, num_q_heads, num_kv_heads, head_dim, max_seq_len, sink_size=4, rw_size=64, h_ratio=0.1,
+                 score_decay=0.999, update_interval=16, k_group_size=16, pbs_metadata_dtype="fp16", device=None):
+        _require_cuda()
+        dev = torch.cuda.current_device() if device is None else torch.device(device).index or 0
+        self._h = None
+        cfg = _lib.EngineConfig(int(num_q_heads), int(num_kv_heads), int(head_dim), int(max_seq_len),
+                                int(sink_size), int(rw_size), float(h_ratio), float(score_decay),
+                                int(update_interval), int(k_group_size),
+                                1 if pbs_metadata_dtype == "fp16" else 0, int(dev))
+        h = C.c_void_p()
+        with torch.cuda.device(dev):
+            check(lib().tt_engine_create(C.byref(cfg), C.byref(h)), "TriTierCacheEngine")
+        self._h = h
+        self._dev = dev
+        self.num_q_heads = int(num_q_heads)
+        self.num_kv_heads = int(num_kv_heads)
+        self.head_dim = int(head_dim)
+        self.max_seq_len = int(max_seq_len)
+        self.sink_size = int(sink_size)
+        self.rw_size = int(rw_size)
+        self.h_ratio = float(np.float32(h_ratio))
+        self.score_decay = float(np.float32(score_decay))
+        self.update_interval = int(update_interval)
+        self.k_group_size = 32 if int(k_group_size) == 32 else 16
+        self.chunk_size = self.k_group_size
+        self.pbs_metadata_dtype = pbs_metadata_dtype
+        self.use_fp16_meta = pbs_metadata_dtype == "fp16"
+        self.quant_head_dim = (self.head_dim + 15) // 16
+        self.device = torch.device("cuda", dev)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            try:
+                lib().tt_engine_destroy(h)
+            except Exception:
+                pass
+            self._h = None
+
+    @property
+    def handle(self) -> int:
+        return self._h.value
+
+    # -- compute --------------------------------------------------------------
+    def step(self, q_ptr, k_ptr, v_ptr, out_ptr):
+        """Ingest one token, attend, update scores (bindings.cpp:399-417)."""
+        kvs = self.num_kv_heads * self.head_dim
+        q = _arg(q_ptr, "Q", self.num_q_heads * self.head_dim * 4)
+        k = _arg(k_ptr, "K_new", kvs * 4)
+        v = _arg(v_ptr, "V_new", kvs * 4)
+        o = _arg(out_ptr, "attn_output", self.num_q_heads * self.head_dim * 4, writable=True)
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_step(self._h, q.ptr, k.ptr, v.ptr, o.ptr, _stream()), "step")
+        _finish(o)
+        self._keep = (q, k, v)
+
+    def prefill(self, k_ptr, v_ptr, q_len):
+        """Batch prompt ingestion (bindings.cpp:418-436)."""
+        if q_len < 0:
+            raise ValueError("q_len must be non-negative.")
+        kvs = self.num_kv_heads * self.head_dim
+        k = _arg(k_ptr, "K_all", q_len * kvs * 4)
+        v = _arg(v_ptr, "V_all", q_len * kvs * 4)
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_prefill(self._h, k.ptr, v.ptr, int(q_len), _stream()), "prefill")
+        self._keep = (k, v)
+
+    # -- state ------------------------------------------------------------------
+    def counters(self) -> dict:
+        c = _lib.EngineCounters()
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_get_counters(self._h, C.byref(c)), "counters")
+        return {n: getattr(c, n) for n, _ in _lib.EngineCounters._fields_}
+
+    def _ctr(self, name):
+        return self.counters()[name]
+
+    s_count = property(lambda self: self._ctr("s_count"))
+    rw_count = property(lambda self: self._ctr("rw_count"))
+    rw_head_index = property(lambda self: self._ctr("rw_head_index"))
+    hh_count = property(lambda self: self._ctr("hh_count"))
+    wr_count = property(lambda self: self._ctr("wr_count"))
+    pbs_count = property(lambda self: self._ctr("pbs_count"))
+    pbs_blocks_used = property(lambda self: self._ctr("pbs_blocks_used"))
+    pbs_allocated_blocks = property(lambda self: self._ctr("pbs_allocated_blocks"))
+    total_processed_tokens = property(lambda self: self._ctr("total_processed_tokens"))
+    total_evictions = property(lambda self: self._ctr("total_evictions"))
+
+    @property
+    def max_hh(self) -> int:
+        return self._ctr("max_hh")
+
+    def get_buffer_bytes(self) -> int:
+        n = C.c_size_t()
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_get_buffer_bytes(self._h, C.byref(n)), "get_buffer_bytes")
+        return int(n.value)
+
+    def get_device_bytes(self) -> int:
+        n = C.c_size_t()
+        check(lib().tt_engine_device_bytes(self._h, C.byref(n)), "get_device_bytes")
+        return int(n.value)
+
+    def _view(self, name: str, shape) -> torch.Tensor:
+        d = _lib.BufferDesc()
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_get_buffer(self._h, _BUF[name], C.byref(d)), name)
+        n = int(np.prod(shape)) if len(shape) else 1
+        if n == 0 or not d.data:
+            dt = {0: torch.float32, 1: torch.int32, 2: torch.int64, 3: torch.uint16}[d.dtype]
+            return torch.empty(tuple(shape), dtype=dt, device=self.device)
+        return torch.as_tensor(_DeviceView(d.data, shape, _TYPESTR[d.dtype], self), device=self.device)
+
+    def get_global_attn_scores(self):
+        return self._view("global_attn_scores", (self.max_seq_len,))
+
+    def get_S_K(self):
+        return self._view("S_K", (self.sink_size, self.num_kv_heads, self.head_dim))
+
+    def get_S_V(self):
+        return self._view("S_V", (self.sink_size, self.num_kv_heads, self.head_dim))
+
+    def get_RW_K(self):
+        return self._view("RW_K", (self.rw_size, self.num_kv_heads, self.head_dim))
+
+    def get_RW_V(self):
+        return self._view("RW_V", (self.rw_size, self.num_kv_heads, self.head_dim))
+
+    def get_HH_K(self):
+        return self._view("HH_K", (self.max_hh, self.num_kv_heads, self.head_dim))
+
+    def get_HH_V(self):
+        return self._view("HH_V", (self.max_hh, self.num_kv_heads, self.head_dim))
+
+    def get_HH_token_ids(self):
+        return self._view("HH_token_ids", (self.max_hh,))
+
+    def get_HH_scores(self):
+        return self._view("HH_scores", (self.max_hh,))
+
+    def get_WR_K(self):
+        return self._view("WR_K", (self.chunk_size, self.num_kv_heads, self.head_dim))
+
+    def get_WR_V(self):
+        return self._view("WR_V", (self.chunk_size, self.num_kv_heads, self.head_dim))
+
+    def get_WR_token_ids(self):
+        return self._view("WR_token_ids", (self.chunk_size,))
+
+    def get_PBS_K_Packed(self):
+        nb = self.pbs_allocated_blocks
+        return self._view("PBS_K_Packed", (nb, self.k_group_size // 16, self.num_kv_heads, self.head_dim))
+
+    def get_PBS_K_Scales(self):
+        return self._view("PBS_K_Scales", (self.pbs_allocated_blocks, self.num_kv_heads, self.head_dim))
+
+    def get_PBS_K_Zeroes(self):
+        return self._view("PBS_K_Zeroes", (self.pbs_allocated_blocks, self.num_kv_heads, self.head_dim))
+
+    def get_PBS_V_Packed(self):
+        return self._view("PBS_V_Packed",
+                          (self.pbs_allocated_blocks * self.chunk_size, self.num_kv_heads, self.quant_head_dim))
+
+    def get_PBS_V_Scales(self):
+        return self._view("PBS_V_Scales", (self.pbs_allocated_blocks * self.chunk_size, self.num_kv_heads, 1))
+
+    def get_PBS_V_Zeroes(self):
+        return self._view("PBS_V_Zeroes", (self.pbs_allocated_blocks * self.chunk_size, self.num_kv_heads, 1))
+
+    def get_PBS_token_ids(self):
+        return self._view("PBS_token_ids", (self.pbs_allocated_blocks * self.chunk_size,))
+
+
+def engine_step_batched(engines, Qs, Ks, Vs, outs) -> None:
+    """One decode step for several engines (layers / sequences) in one set of
+    launches.  Every argument is a sequence of CUDA tensors (contiguous FP32);
+    no reference counterpart (the reference is batch-1, one engine per call)."""
+    n = len(engines)
+    if not (len(Qs) == len(Ks) == len(Vs) == len(outs) == n):
+        raise ValueError("engine_step_batched: argument lengths differ.")
+    arr = C.c_void_p * n
+    hs = arr(*[e._h.value for e in engines])
+
+    def ptrs(ts, name):
+        out = []
+        for t in ts:
+            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous()):
+                raise ValueError(f"engine_step_batched: {name} entries must be contiguous CUDA tensors.")
+            out.append(t.data_ptr())
+        return arr(*out)
+
+    with torch.cuda.device(engines[0]._dev):
+        check(lib().tt_engine_step_batched(hs, n, ptrs(Qs, "Q"), ptrs(Ks, "K_new"), ptrs(Vs, "V_new"),
+                                           ptrs(outs, "attn_output"), _stream()), "engine_step_batched")

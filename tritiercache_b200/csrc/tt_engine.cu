@@ -1,0 +1,862 @@
+// tt_engine.cu -- device-resident TriTierCache engine.
+//
+// Replaces TriTierCacheEngine (csrc/cache_engine.cpp).  All tier buffers and
+// counters live in HBM; one decode step is three stream-ordered launches for
+// any number of engines (layers / sequences):
+//   k_engine_maintain  one CTA per engine: ingest the new token into the
+//                      sink / recent-window ring, evict the oldest ring slot,
+//                      route it (radix-select percentile threshold every
+//                      update_interval tokens, heavy-hitter append or
+//                      strict-argmin replace with demotion), and flush a full
+//                      waiting room into one packed block (bit-exact
+//                      quantize+pack).  cache_engine.cpp:118-269, :397-431.
+//   k_attn_partial / k_attn_finalize (tt_attn.cu) over the tiers in place
+//                      (no dense re-assembly, cache_engine.cpp:433-459),
+//                      with the decayed score feedback fused into the
+//                      finalize pass (cache_engine.cpp:511-540).
+// The host never waits for the device inside step(); the integer state the
+// host needs for grid sizing is either deterministic (token counts) or an
+// upper bound (packed blocks).
+#include <algorithm>
+#include <new>
+#include <string.h>
+#include <vector>
+
+#include "tt_attn.cuh"
+
+using namespace tt;
+
+struct tt_engine {
+    tt_engine_config cfg;
+    int chunk, qhd, max_hh;
+    size_t kvs;
+    int meta_bytes;
+    // device buffers
+    float *S_K = nullptr, *S_V = nullptr, *RW_K = nullptr, *RW_V = nullptr, *HH_K = nullptr, *HH_V = nullptr;
+    float *HH_scores = nullptr, *WR_K = nullptr, *WR_V = nullptr, *g = nullptr;
+    int64_t *HH_ids = nullptr, *WR_ids = nullptr, *PBS_ids = nullptr;
+    int32_t *kp = nullptr, *vp = nullptr;
+    void *ks = nullptr, *kz = nullptr, *vs = nullptr, *vz = nullptr;
+    int pbs_cap = 0;  // physical packed blocks
+    DevCounters* ctr = nullptr;
+    float* scratch = nullptr;
+    size_t scratch_floats = 0;
+    JobDesc* job_dev = nullptr;
+    void* maint_dev = nullptr;
+    // host mirrors: exact (token-count driven) and upper bounds
+    int h_total = 0, h_s = 0, h_rw = 0, h_rw_head = 0, h_evictions = 0;
+    long long h_wr_pbs_ub = 0;  // upper bound of tokens in waiting room + PBS
+    cudaStream_t last_stream = nullptr;
+};
+
+namespace tt {
+
+// Per-engine constants and pointers read by the maintenance kernel.
+struct MaintDesc {
+    int nkv, hd, msl, S, R, ui, grp, meta16, max_hh, qhd, pbs_cap;
+    float h_ratio;
+    size_t kvs;
+    float *S_K, *S_V, *RW_K, *RW_V, *HH_K, *HH_V, *HH_scores, *WR_K, *WR_V, *g;
+    int64_t *HH_ids, *WR_ids, *PBS_ids;
+    int32_t *kp, *vp;
+    void *ks, *kz, *vs, *vz;
+    DevCounters* ctr;
+};
+
+struct MaintBatch {
+    int n;
+    const MaintDesc* d[kMaxBatch];
+    const float* K[kMaxBatch];
+    const float* V[kMaxBatch];
+};
+
+constexpr int MT = 512;  // maintenance CTA size
+
+__device__ __forceinline__ void copy_row(float* __restrict__ dst, const float* __restrict__ src, size_t n) {
+    if ((((uintptr_t)dst | (uintptr_t)src) & 15) == 0 && (n & 3) == 0) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        for (size_t i = threadIdx.x; i < n / 4; i += blockDim.x) d4[i] = s4[i];
+    } else {
+        for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+    }
+}
+
+__device__ __forceinline__ uint32_t order_key(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// k-th smallest (0-based) of x[0..n): 4 passes of an 8-bit radix histogram.
+// Returns the same value as std::nth_element (cache_engine.cpp:140-141).
+__device__ float block_select_kth(const float* __restrict__ x, int n, int k, unsigned int* hist) {
+    __shared__ uint32_t s_prefix, s_k;
+    uint32_t prefix = 0, mask = 0;
+    if (threadIdx.x == 0) s_k = (uint32_t)k;
+    for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint32_t key = order_key(x[i]);
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint32_t kk = s_k, cum = 0, d = 0;
+            for (d = 0; d < 256; ++d) {
+                if (kk < cum + hist[d]) break;
+                cum += hist[d];
+            }
+            if (d > 255) d = 255;
+            s_k = kk - cum;
+            s_prefix = prefix | (d << shift);
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        mask |= 255u << shift;
+        __syncthreads();
+    }
+    return key_value(prefix);
+}
+
+// quantize the full waiting room into packed block `b` (cache_engine.cpp:148-207)
+__device__ void flush_waiting_room(const MaintDesc& E, DevCounters& c) {
+    const int b = c.pbs_used;
+    if (b >= E.pbs_cap) {  // the host sizes the PBS from an upper bound; never expected
+        if (threadIdx.x == 0) c.error = TT_ERR_OUT_OF_RANGE;
+        __syncthreads();
+        return;
+    }
+    if (threadIdx.x == 0 && b + 1 > c.pbs_alloc) c.pbs_alloc = max(c.pbs_alloc + 64, b + 1);  // :84-116
+    const size_t words = (size_t)E.grp / 16;
+    const size_t mbytes = E.meta16 ? 2 : 4;
+    quantize_k_block_dev(E.WR_K, reinterpret_cast<uint32_t*>(E.kp) + (size_t)b * words * E.kvs,
+                         (char*)E.ks + (size_t)b * E.kvs * mbytes, (char*)E.kz + (size_t)b * E.kvs * mbytes,
+                         E.meta16, E.nkv, E.hd, E.grp, threadIdx.x, blockDim.x);
+    const size_t vm = (size_t)b * E.grp * E.nkv;
+    quantize_v_block_dev(E.WR_V, E.vp + vm * E.qhd, (char*)E.vs + vm * mbytes, (char*)E.vz + vm * mbytes, E.meta16,
+                         E.nkv, E.hd, E.grp, threadIdx.x, blockDim.x);
+    for (int t = threadIdx.x; t < E.grp; t += blockDim.x) E.PBS_ids[(size_t)b * E.grp + t] = E.WR_ids[t];
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        c.pbs_used = b + 1;
+        c.pbs_count += E.grp;
+        c.wr_count = 0;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ MaintBatch B) {
+    __shared__ MaintDesc E;
+    __shared__ DevCounters c;
+    __shared__ unsigned int hist[256];
+    __shared__ float s_red_v[MT / 32];
+    __shared__ int s_red_i[MT / 32];
+    __shared__ int s_action, s_mi;
+    __shared__ float s_score;
+    if (threadIdx.x == 0) {
+        E = *B.d[blockIdx.x];
+        c = *E.ctr;
+    }
+    __syncthreads();
+    const float* Kn = B.K[blockIdx.x];
+    const float* Vn = B.V[blockIdx.x];
+    const size_t kvs = E.kvs;
+
+    if (c.s_count < E.S) {  // :406-409
+        copy_row(E.S_K + (size_t)c.s_count * kvs, Kn, kvs);
+        copy_row(E.S_V + (size_t)c.s_count * kvs, Vn, kvs);
+        __syncthreads();
+        if (threadIdx.x == 0) c.s_count++;
+    } else if (c.rw_count < E.R) {  // :410-413
+        copy_row(E.RW_K + (size_t)c.rw_count * kvs, Kn, kvs);
+        copy_row(E.RW_V + (size_t)c.rw_count * kvs, Vn, kvs);
+        __syncthreads();
+        if (threadIdx.x == 0) c.rw_count++;
+    } else {
+        // ---- ring eviction (:414-430) and routing (:209-269) ----
+        const int slot = c.rw_head;
+        const long long id = (long long)c.total - E.R;
+        const float* ek = E.RW_K + (size_t)slot * kvs;
+        const float* ev = E.RW_V + (size_t)slot * kvs;
+        // threshold (:118-146); candidates clamped to the score buffer
+        const int cs = E.S, ce = c.total - E.R;
+        if (ce <= cs) {
+            if (threadIdx.x == 0) c.cached_threshold = 0.f;
+        } else if (c.last_calc_pos == -1 || (c.total - c.last_calc_pos >= E.ui)) {
+            const int n = ce - cs;
+            float q = 1.0f - E.h_ratio;
+            q = q < 0.f ? 0.f : (q > 1.f ? 1.f : q);
+            const int k = (int)(size_t)(q * (float)(n - 1));
+            const int nread = min(ce, E.msl) - cs;
+            const float v = nread > 0 ? block_select_kth(E.g + cs, nread, min(k, nread - 1), hist) : 0.f;
+            if (threadIdx.x == 0) {
+                c.cached_threshold = v;
+                c.last_calc_pos = c.total;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            c.total_evictions++;
+            s_score = (id >= 0 && id < E.msl) ? E.g[id] : 0.f;
+        }
+        __syncthreads();
+        const float score = s_score, thresh = c.cached_threshold;
+        int action = 2;  // 0: HH append, 1: HH replace + demote, 2: waiting room
+        int mi = 0;
+        if (score >= thresh) {
+            if (c.hh_count < E.max_hh) {
+                action = 0;
+            } else {
+                // strict-< argmin, first index wins (:231-238)
+                float bv = INFINITY;
+                int bi = 0x7fffffff;  // "none"
+                for (int i = threadIdx.x; i < c.hh_count; i += blockDim.x) {
+                    const float v = E.HH_scores[i];
+                    if (bi == 0x7fffffff || v < bv) { bv = v; bi = i; }  // i ascends: ties keep the first
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (oi != 0x7fffffff && (bi == 0x7fffffff || ov < bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+                }
+                if ((threadIdx.x & 31) == 0) { s_red_v[threadIdx.x >> 5] = bv; s_red_i[threadIdx.x >> 5] = bi; }
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    float v0 = INFINITY;
+                    int i0 = 0x7fffffff;
+                    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+                        const int oi = s_red_i[w];
+                        const float ov = s_red_v[w];
+                        if (oi != 0x7fffffff && (i0 == 0x7fffffff || ov < v0 || (ov == v0 && oi < i0))) { v0 = ov; i0 = oi; }
+                    }
+                    s_mi = i0;
+                    s_action = (score > v0) ? 1 : 2;
+                }
+                __syncthreads();
+                action = s_action;
+                mi = s_mi;
+            }
+        }
+        if (action == 0) {
+            const int h = c.hh_count;
+            copy_row(E.HH_K + (size_t)h * kvs, ek, kvs);
+            copy_row(E.HH_V + (size_t)h * kvs, ev, kvs);
+            if (threadIdx.x == 0) {
+                E.HH_ids[h] = id;
+                E.HH_scores[h] = score;
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) c.hh_count = h + 1;
+        } else if (action == 1) {
+            const int w = c.wr_count;
+            copy_row(E.WR_K + (size_t)w * kvs, E.HH_K + (size_t)mi * kvs, kvs);
+            copy_row(E.WR_V + (size_t)w * kvs, E.HH_V + (size_t)mi * kvs, kvs);
+            if (threadIdx.x == 0) E.WR_ids[w] = E.HH_ids[mi];
+            __syncthreads();
+            copy_row(E.HH_K + (size_t)mi * kvs, ek, kvs);
+            copy_row(E.HH_V + (size_t)mi * kvs, ev, kvs);
+            if (threadIdx.x == 0) {
+                E.HH_ids[mi] = id;
+                E.HH_scores[mi] = score;
+                c.wr_count = w + 1;
+            }
+            __syncthreads();
+        } else {
+            const int w = c.wr_count;
+            copy_row(E.WR_K + (size_t)w * kvs, ek, kvs);
+            copy_row(E.WR_V + (size_t)w * kvs, ev, kvs);
+            if (threadIdx.x == 0) {
+                E.WR_ids[w] = id;
+                c.wr_count = w + 1;
+            }
+            __syncthreads();
+        }
+        __syncthreads();
+        if (c.wr_count == E.grp) flush_waiting_room(E, c);
+        // overwrite the ring slot with the new token (:424-428)
+        copy_row(E.RW_K + (size_t)slot * kvs, Kn, kvs);
+        copy_row(E.RW_V + (size_t)slot * kvs, Vn, kvs);
+        __syncthreads();
+        if (threadIdx.x == 0) c.rw_head = (c.rw_head + 1) % E.R;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        c.total++;
+        *E.ctr = c;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// prefill (cache_engine.cpp:271-395)
+// ---------------------------------------------------------------------------
+// grid = blocks to quantize; block b reads tokens [S + b*C, +C) into packed
+// block (pbs_used + b).
+__global__ void __launch_bounds__(256) k_prefill_quantize(const MaintDesc* __restrict__ Ed, const float* K_all,
+                                                         const float* V_all) {
+    const MaintDesc& E = *Ed;
+    const int base = E.ctr->pbs_used;
+    const int b = blockIdx.x;
+    const int dst = base + b;
+    if (dst >= E.pbs_cap) return;
+    const int src = E.S + b * E.grp;
+    const size_t words = (size_t)E.grp / 16;
+    const size_t mbytes = E.meta16 ? 2 : 4;
+    quantize_k_block_dev(K_all + (size_t)src * E.kvs, reinterpret_cast<uint32_t*>(E.kp) + (size_t)dst * words * E.kvs,
+                         (char*)E.ks + (size_t)dst * E.kvs * mbytes, (char*)E.kz + (size_t)dst * E.kvs * mbytes,
+                         E.meta16, E.nkv, E.hd, E.grp, threadIdx.x, blockDim.x);
+    const size_t vm = (size_t)dst * E.grp * E.nkv;
+    quantize_v_block_dev(V_all + (size_t)src * E.kvs, E.vp + vm * E.qhd, (char*)E.vs + vm * mbytes,
+                         (char*)E.vz + vm * mbytes, E.meta16, E.nkv, E.hd, E.grp, threadIdx.x, blockDim.x);
+    for (int t = threadIdx.x; t < E.grp; t += blockDim.x) E.PBS_ids[(size_t)dst * E.grp + t] = src + t;
+}
+
+// tier copies and counter updates; runs after k_prefill_quantize
+__global__ void __launch_bounds__(512) k_prefill_finish(const MaintDesc* __restrict__ Ed, const float* K_all,
+                                                       const float* V_all, int q_len, int nblk) {
+    const MaintDesc& E = *Ed;
+    __shared__ DevCounters c;
+    if (threadIdx.x == 0) c = *E.ctr;
+    __syncthreads();
+    const size_t kvs = E.kvs;
+    if (q_len <= E.S + E.R) {
+        const int s = min(E.S, q_len);
+        if (s > 0) {
+            copy_row(E.S_K, K_all, (size_t)s * kvs);
+            copy_row(E.S_V, V_all, (size_t)s * kvs);
+        }
+        const int r = q_len - s;
+        if (r > 0) {
+            copy_row(E.RW_K, K_all + (size_t)s * kvs, (size_t)r * kvs);
+            copy_row(E.RW_V, V_all + (size_t)s * kvs, (size_t)r * kvs);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            if (s > 0) c.s_count = s;
+            if (r > 0) { c.rw_count = r; c.rw_head = 0; }
+            c.total = q_len;
+            *E.ctr = c;
+        }
+        return;
+    }
+    copy_row(E.S_K, K_all, (size_t)E.S * kvs);
+    copy_row(E.S_V, V_all, (size_t)E.S * kvs);
+    const int rw_start = q_len - E.R;
+    copy_row(E.RW_K, K_all + (size_t)rw_start * kvs, (size_t)E.R * kvs);
+    copy_row(E.RW_V, V_all + (size_t)rw_start * kvs, (size_t)E.R * kvs);
+    const int n_inter = rw_start - E.S;
+    const int rem = n_inter - nblk * E.grp;
+    if (rem > 0) {
+        const int rs = E.S + nblk * E.grp;
+        copy_row(E.WR_K, K_all + (size_t)rs * kvs, (size_t)rem * kvs);
+        copy_row(E.WR_V, V_all + (size_t)rs * kvs, (size_t)rem * kvs);
+        for (int t = threadIdx.x; t < rem; t += blockDim.x) E.WR_ids[t] = rs + t;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        c.s_count = E.S;
+        c.rw_count = E.R;
+        c.rw_head = 0;
+        if (nblk > 0) {
+            const int need = c.pbs_used + nblk;
+            if (need > E.pbs_cap) c.error = TT_ERR_OUT_OF_RANGE;
+            if (need > c.pbs_alloc) c.pbs_alloc = max(c.pbs_alloc + 64, need);
+            c.pbs_used = need;
+            c.pbs_count += nblk * E.grp;
+            c.total_evictions += nblk * E.grp;
+        }
+        c.wr_count = rem > 0 ? rem : 0;
+        c.total = q_len;
+        *E.ctr = c;
+    }
+}
+
+__global__ void k_fill_i64(int64_t* p, size_t n, int64_t v) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+}  // namespace tt
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+template <typename T>
+tt_status dalloc(T** p, size_t n, const char* what) {
+    *p = nullptr;
+    if (n == 0) n = 1;
+    tt_status s = check_cuda(cudaMalloc((void**)p, n * sizeof(T)), what);
+    if (s != TT_OK) return s;
+    return check_cuda(cudaMemset(*p, 0, n * sizeof(T)), what);
+}
+
+constexpr int kLogicalSlack = 64;
+
+int dense_cap(const tt_engine* e) { return e->cfg.sink_size + e->max_hh + e->cfg.rw_size; }
+
+void free_pbs(tt_engine* e) {
+    cudaFree(e->kp); cudaFree(e->vp); cudaFree(e->ks); cudaFree(e->kz); cudaFree(e->vs); cudaFree(e->vz);
+    cudaFree(e->PBS_ids);
+    e->kp = e->vp = nullptr;
+    e->ks = e->kz = e->vs = e->vz = nullptr;
+    e->PBS_ids = nullptr;
+}
+
+tt_status write_descriptors(tt_engine* e) {
+    MaintDesc md;
+    md.nkv = e->cfg.num_kv_heads; md.hd = e->cfg.head_dim; md.msl = e->cfg.max_seq_len; md.S = e->cfg.sink_size;
+    md.R = e->cfg.rw_size; md.ui = e->cfg.update_interval; md.grp = e->chunk; md.meta16 = e->cfg.meta_fp16;
+    md.max_hh = e->max_hh; md.qhd = e->qhd; md.pbs_cap = e->pbs_cap; md.h_ratio = e->cfg.h_ratio; md.kvs = e->kvs;
+    md.S_K = e->S_K; md.S_V = e->S_V; md.RW_K = e->RW_K; md.RW_V = e->RW_V; md.HH_K = e->HH_K; md.HH_V = e->HH_V;
+    md.HH_scores = e->HH_scores; md.WR_K = e->WR_K; md.WR_V = e->WR_V; md.g = e->g;
+    md.HH_ids = e->HH_ids; md.WR_ids = e->WR_ids; md.PBS_ids = e->PBS_ids;
+    md.kp = e->kp; md.vp = e->vp; md.ks = e->ks; md.kz = e->kz; md.vs = e->vs; md.vz = e->vz; md.ctr = e->ctr;
+
+    JobDesc j;
+    memset(&j, 0, sizeof(j));
+    j.nq = e->cfg.num_q_heads; j.nkv = e->cfg.num_kv_heads; j.hd = e->cfg.head_dim; j.grp = e->chunk;
+    j.meta16 = e->cfg.meta_fp16; j.ring_size = e->cfg.rw_size;
+    j.K0 = e->S_K; j.V0 = e->S_V; j.K1 = e->HH_K; j.V1 = e->HH_V; j.K2 = e->RW_K; j.V2 = e->RW_V;
+    j.kp = e->kp; j.ks = e->ks; j.kz = e->kz; j.vp = e->vp; j.vs = e->vs; j.vz = e->vz; j.ids = e->PBS_ids;
+    j.ctr = e->ctr;
+    const int maxch = attn_max_chunks(dense_cap(e), e->pbs_cap * e->chunk);
+    j.max_chunks = maxch;
+    j.score_stride = dense_cap(e) + e->pbs_cap * e->chunk;
+    j.part_ml = e->scratch;
+    j.part_acc = e->scratch + (size_t)maxch * j.nq * 2;
+    j.scores = j.part_acc + (size_t)maxch * j.nq * j.hd;
+    j.g = e->g; j.hh_scores = e->HH_scores; j.hh_ids = e->HH_ids; j.decay = e->cfg.score_decay;
+    j.msl = e->cfg.max_seq_len;
+    tt_status s = check_cuda(cudaMemcpy(e->maint_dev, &md, sizeof(md), cudaMemcpyHostToDevice), "descriptor upload");
+    if (s != TT_OK) return s;
+    return check_cuda(cudaMemcpy(e->job_dev, &j, sizeof(j), cudaMemcpyHostToDevice), "descriptor upload");
+}
+
+size_t scratch_need(const tt_engine* e, int pbs_cap) {
+    const int maxch = attn_max_chunks(dense_cap(e), pbs_cap * e->chunk);
+    const size_t stride = (size_t)dense_cap(e) + (size_t)pbs_cap * e->chunk;
+    return (size_t)maxch * e->cfg.num_q_heads * (e->cfg.head_dim + 2) + (size_t)e->cfg.num_q_heads * stride + 64;
+}
+
+// (Re)allocates packed storage for `blocks` physical blocks, preserving
+// the first `keep` blocks.  Synchronises the device (rare: the initial
+// capacity covers max_seq_len tokens).
+tt_status grow_pbs(tt_engine* e, int blocks) {
+    const int old = e->pbs_cap;
+    const size_t kvs = e->kvs, C = e->chunk, words = C / 16, mb = e->meta_bytes;
+    const size_t vrow = (size_t)e->cfg.num_kv_heads * e->qhd;
+    int32_t *kp, *vp;
+    void *ks, *kz, *vs, *vz;
+    int64_t* ids;
+    tt_status s;
+    if ((s = check_cuda(cudaDeviceSynchronize(), "PBS growth")) != TT_OK) return s;
+    if ((s = dalloc(&kp, (size_t)blocks * words * kvs, "PBS_K_Packed")) != TT_OK) return s;
+    if ((s = dalloc((char**)&ks, (size_t)blocks * kvs * mb, "PBS_K_Scales")) != TT_OK) return s;
+    if ((s = dalloc((char**)&kz, (size_t)blocks * kvs * mb, "PBS_K_Zeroes")) != TT_OK) return s;
+    if ((s = dalloc(&vp, (size_t)blocks * C * vrow, "PBS_V_Packed")) != TT_OK) return s;
+    if ((s = dalloc((char**)&vs, (size_t)blocks * C * e->cfg.num_kv_heads * mb, "PBS_V_Scales")) != TT_OK) return s;
+    if ((s = dalloc((char**)&vz, (size_t)blocks * C * e->cfg.num_kv_heads * mb, "PBS_V_Zeroes")) != TT_OK) return s;
+    if ((s = dalloc(&ids, (size_t)blocks * C, "PBS_token_ids")) != TT_OK) return s;
+    k_fill_i64<<<64, 256>>>(ids, (size_t)blocks * C, -1);
+    if (old > 0) {
+        cudaMemcpy(kp, e->kp, (size_t)old * words * kvs * 4, cudaMemcpyDeviceToDevice);
+        cudaMemcpy(ks, e->ks, (size_t)old * kvs * mb, cudaMemcpyDeviceToDevice);
+        cudaMemcpy(kz, e->kz, (size_t)old * kvs * mb, cudaMemcpyDeviceToDevice);
+        cudaMemcpy(vp, e->vp, (size_t)old * C * vrow * 4, cudaMemcpyDeviceToDevice);
+        cudaMemcpy(vs, e->vs, (size_t)old * C * e->cfg.num_kv_heads * mb, cudaMemcpyDeviceToDevice);
+        cudaMemcpy(vz, e->vz, (size_t)old * C * e->cfg.num_kv_heads * mb, cudaMemcpyDeviceToDevice);
+        cudaMemcpy(ids, e->PBS_ids, (size_t)old * C * 8, cudaMemcpyDeviceToDevice);
+    }
+    free_pbs(e);
+    e->kp = kp; e->ks = ks; e->kz = kz; e->vp = vp; e->vs = vs; e->vz = vz; e->PBS_ids = ids;
+    e->pbs_cap = blocks;
+    const size_t need = scratch_need(e, blocks);
+    if (need > e->scratch_floats) {
+        cudaFree(e->scratch);
+        e->scratch = nullptr;
+        if ((s = dalloc(&e->scratch, need, "attention scratch")) != TT_OK) return s;
+        e->scratch_floats = need;
+    }
+    if ((s = check_launch("PBS id init")) != TT_OK) return s;
+    return write_descriptors(e);
+}
+
+// Makes sure a step (extra_tokens = 1) or a prefill cannot run out of packed blocks.
+tt_status ensure_capacity(tt_engine* e, long long wr_pbs_tokens_after) {
+    // the reference grows its logical allocation by +64 blocks (cache_engine.cpp:84-116), so the
+    // logical view (pbs_allocated_blocks) can run up to 63 blocks past the blocks in use
+    const long long blocks = wr_pbs_tokens_after / e->chunk + 1 + kLogicalSlack;
+    if (blocks <= e->pbs_cap) return TT_OK;
+    long long nb = std::max<long long>(blocks, (long long)e->pbs_cap + e->pbs_cap / 4 + 64);
+    if (nb > (1LL << 30) / std::max<size_t>(1, e->kvs)) return set_error(TT_ERR_OUT_OF_MEMORY, "PBS capacity overflow");
+    return grow_pbs(e, (int)nb);
+}
+
+tt_status validate(const tt_engine* e) {
+    if (!e) return set_error(TT_ERR_INVALID_ARGUMENT, "engine handle is NULL.");
+    return TT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+tt_status tt_engine_create(const tt_engine_config* cfg, tt_engine** out) {
+    if (!cfg || !out) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    *out = nullptr;
+    const tt_engine_config& c = *cfg;
+    if (c.num_q_heads <= 0 || c.num_kv_heads <= 0 || c.head_dim <= 0 || c.max_seq_len <= 0)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "num_q_heads, num_kv_heads, head_dim and max_seq_len must be positive.");
+    if (c.sink_size < 0 || c.rw_size <= 0)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "sink_size must be >= 0 and rw_size > 0.");
+    if (c.update_interval < 0) return set_error(TT_ERR_INVALID_ARGUMENT, "update_interval must be >= 0.");
+    if (c.head_dim % 16 != 0)
+        return set_error(TT_ERR_UNSUPPORTED, "head_dim must be a multiple of 16 (packed V rows).");
+    AttnLaunch probe;
+    memset(&probe, 0, sizeof(probe));
+    probe.njobs = 1;
+    tt_status s = plan_attention(probe, c.num_q_heads, c.num_kv_heads, c.head_dim, 1, 1);
+    if (s != TT_OK) return s;
+
+    DeviceGuard dg(c.device);
+    tt_engine* e = new (std::nothrow) tt_engine();
+    if (!e) return set_error(TT_ERR_OUT_OF_MEMORY, "engine allocation failed");
+    e->cfg = c;
+    e->cfg.k_group_size = (c.k_group_size == 32) ? 32 : 16;  // cache_engine.cpp:29
+    e->cfg.meta_fp16 = c.meta_fp16 ? 1 : 0;
+    e->chunk = e->cfg.k_group_size;
+    e->qhd = (c.head_dim + 15) / 16;
+    e->max_hh = (int)ceilf((float)c.max_seq_len * c.h_ratio);  // :47-48
+    if (e->max_hh < 1) e->max_hh = 1;
+    e->kvs = (size_t)c.num_kv_heads * c.head_dim;
+    e->meta_bytes = e->cfg.meta_fp16 ? 2 : 4;
+    const size_t kvs = e->kvs;
+#define TT_TRY(x)                     \
+    do {                              \
+        tt_status _s = (x);           \
+        if (_s != TT_OK) {            \
+            tt_engine_destroy(e);     \
+            return _s;                \
+        }                             \
+    } while (0)
+    TT_TRY(dalloc(&e->S_K, (size_t)std::max(c.sink_size, 1) * kvs, "S_K"));
+    TT_TRY(dalloc(&e->S_V, (size_t)std::max(c.sink_size, 1) * kvs, "S_V"));
+    TT_TRY(dalloc(&e->RW_K, (size_t)c.rw_size * kvs, "RW_K"));
+    TT_TRY(dalloc(&e->RW_V, (size_t)c.rw_size * kvs, "RW_V"));
+    TT_TRY(dalloc(&e->HH_K, (size_t)e->max_hh * kvs, "HH_K"));
+    TT_TRY(dalloc(&e->HH_V, (size_t)e->max_hh * kvs, "HH_V"));
+    TT_TRY(dalloc(&e->HH_scores, (size_t)e->max_hh, "HH_scores"));
+    TT_TRY(dalloc(&e->HH_ids, (size_t)e->max_hh, "HH_token_ids"));
+    TT_TRY(dalloc(&e->WR_K, (size_t)e->chunk * kvs, "WR_K"));
+    TT_TRY(dalloc(&e->WR_V, (size_t)e->chunk * kvs, "WR_V"));
+    TT_TRY(dalloc(&e->WR_ids, (size_t)e->chunk, "WR_token_ids"));
+    TT_TRY(dalloc(&e->g, (size_t)c.max_seq_len, "global_attn_scores"));
+    TT_TRY(dalloc(&e->ctr, 1, "counters"));
+    TT_TRY(dalloc((char**)&e->maint_dev, sizeof(MaintDesc), "descriptor"));
+    TT_TRY(dalloc((char**)&e->job_dev, sizeof(JobDesc), "descriptor"));
+    k_fill_i64<<<8, 256>>>(e->HH_ids, (size_t)e->max_hh, -1);
+    k_fill_i64<<<1, 64>>>(e->WR_ids, (size_t)e->chunk, -1);
+    TT_TRY(check_launch("engine init"));
+    DevCounters dc;
+    memset(&dc, 0, sizeof(dc));
+    dc.last_calc_pos = -1;
+    TT_TRY(check_cuda(cudaMemcpy(e->ctr, &dc, sizeof(dc), cudaMemcpyHostToDevice), "counter init"));
+    // packed capacity for max_seq_len tokens up front; grows only beyond that
+    TT_TRY(grow_pbs(e, c.max_seq_len / e->chunk + 2 + kLogicalSlack));
+    TT_TRY(check_cuda(cudaDeviceSynchronize(), "engine create"));
+#undef TT_TRY
+    *out = e;
+    return TT_OK;
+}
+
+tt_status tt_engine_destroy(tt_engine* e) {
+    if (!e) return TT_OK;
+    DeviceGuard dg(e->cfg.device);
+    cudaDeviceSynchronize();
+    float* fl[] = {e->S_K, e->S_V, e->RW_K, e->RW_V, e->HH_K, e->HH_V, e->HH_scores, e->WR_K, e->WR_V, e->g, e->scratch};
+    for (float* p : fl) cudaFree(p);
+    cudaFree(e->HH_ids); cudaFree(e->WR_ids); cudaFree(e->ctr); cudaFree(e->job_dev); cudaFree(e->maint_dev);
+    free_pbs(e);
+    delete e;
+    return TT_OK;
+}
+
+tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* const* Q, const float* const* K_new,
+                                 const float* const* V_new, float* const* attn_output, void* stream) {
+    if (n <= 0) return TT_OK;
+    if (!engines || !Q || !K_new || !V_new || !attn_output) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    for (int i = 0; i < n; ++i) {
+        tt_status s = validate(engines[i]);
+        if (s != TT_OK) return s;
+        if (!Q[i] || !K_new[i] || !V_new[i] || !attn_output[i])
+            return set_error(TT_ERR_INVALID_ARGUMENT, "Q, K_new, V_new and attn_output must not be NULL.");
+        const tt_engine_config& a = engines[i]->cfg;
+        const tt_engine_config& b = engines[0]->cfg;
+        if (a.num_q_heads != b.num_q_heads || a.num_kv_heads != b.num_kv_heads || a.head_dim != b.head_dim ||
+            a.device != b.device)
+            return set_error(TT_ERR_INVALID_ARGUMENT, "batched engines must share heads, head_dim and device.");
+        if (((uintptr_t)Q[i] & 15) || ((uintptr_t)K_new[i] & 15) || ((uintptr_t)V_new[i] & 15))
+            return set_error(TT_ERR_INVALID_ARGUMENT, "Q, K_new and V_new must be 16-byte aligned.");
+    }
+    DeviceGuard dg(engines[0]->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    for (int base = 0; base < n; base += kMaxBatch) {
+        const int m = std::min(kMaxBatch, n - base);
+        MaintBatch mb;
+        memset(&mb, 0, sizeof(mb));
+        mb.n = m;
+        int dcap = 0, pcap = 0;
+        for (int i = 0; i < m; ++i) {
+            tt_engine* e = engines[base + i];
+            // host mirrors: does this step evict?
+            const bool evicts = !(e->h_s < e->cfg.sink_size) && !(e->h_rw < e->cfg.rw_size);
+            if (evicts) {
+                tt_status s = ensure_capacity(e, e->h_wr_pbs_ub + 1);
+                if (s != TT_OK) return s;
+            }
+            mb.d[i] = reinterpret_cast<const MaintDesc*>(e->maint_dev);
+            mb.K[i] = K_new[base + i];
+            mb.V[i] = V_new[base + i];
+            dcap = std::max(dcap, dense_cap(e));
+            const long long ub_blocks = (e->h_wr_pbs_ub + (evicts ? 1 : 0)) / e->chunk;
+            pcap = std::max<long long>(pcap, std::min<long long>(ub_blocks, e->pbs_cap) * e->chunk);
+        }
+        const int ps = prof_begin(0, st);
+        k_engine_maintain<<<m, MT, 0, st>>>(mb);
+        prof_end(ps, st);
+        tt_status s = check_launch("k_engine_maintain");
+        if (s != TT_OK) return s;
+
+        AttnLaunch L;
+        memset(&L, 0, sizeof(L));
+        L.njobs = m;
+        const tt_engine_config& c0 = engines[base]->cfg;
+        s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, dcap, pcap);
+        if (s != TT_OK) return s;
+        L.inline_job.hd = c0.head_dim;
+        L.inline_job.nq = c0.num_q_heads;
+        for (int i = 0; i < m; ++i) {
+            tt_engine* e = engines[base + i];
+            L.jobs[i] = e->job_dev;
+            L.Q[i] = Q[base + i];
+            L.out[i] = attn_output[base + i];
+            L.mw[i] = nullptr;
+        }
+        s = launch_attention(L, st);
+        if (s != TT_OK) return s;
+        for (int i = 0; i < m; ++i) {
+            tt_engine* e = engines[base + i];
+            if (e->h_s < e->cfg.sink_size) {
+                e->h_s++;
+            } else if (e->h_rw < e->cfg.rw_size) {
+                e->h_rw++;
+            } else {
+                e->h_rw_head = (e->h_rw_head + 1) % e->cfg.rw_size;
+                e->h_evictions++;
+                e->h_wr_pbs_ub++;
+            }
+            e->h_total++;
+            e->last_stream = st;
+        }
+    }
+    return TT_OK;
+}
+
+tt_status tt_engine_step(tt_engine* e, const float* Q, const float* K_new, const float* V_new, float* attn_output,
+                         void* stream) {
+    return tt_engine_step_batched(&e, 1, &Q, &K_new, &V_new, &attn_output, stream);
+}
+
+tt_status tt_engine_prefill(tt_engine* e, const float* K_all, const float* V_all, int q_len, void* stream) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (q_len < 0) return set_error(TT_ERR_INVALID_ARGUMENT, "q_len must be non-negative.");
+    if (q_len > 0 && (!K_all || !V_all)) return set_error(TT_ERR_INVALID_ARGUMENT, "K_all/V_all must not be NULL.");
+    DeviceGuard dg(e->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int S = e->cfg.sink_size, R = e->cfg.rw_size;
+    int nblk = 0;
+    if (q_len > S + R) {
+        const int n_inter = q_len - R - S;
+        nblk = n_inter / e->chunk;
+        const int rem = n_inter % e->chunk;
+        // WR is overwritten (rem tokens) and nblk blocks are appended
+        const long long ub_pbs = (e->h_wr_pbs_ub / e->chunk) * e->chunk + (long long)nblk * e->chunk;
+        s = ensure_capacity(e, ub_pbs + rem);
+        if (s != TT_OK) return s;
+        if (nblk > 0) {
+            k_prefill_quantize<<<nblk, 256, 0, st>>>(reinterpret_cast<const MaintDesc*>(e->maint_dev), K_all, V_all);
+            if ((s = check_launch("k_prefill_quantize")) != TT_OK) return s;
+        }
+        e->h_s = S;
+        e->h_rw = R;
+        e->h_rw_head = 0;
+        e->h_evictions += nblk * e->chunk;
+        e->h_wr_pbs_ub = ub_pbs + rem;
+    } else {
+        const int sc = std::min(S, q_len);
+        if (sc > 0) e->h_s = sc;
+        if (q_len - sc > 0) {
+            e->h_rw = q_len - sc;
+            e->h_rw_head = 0;
+        }
+    }
+    k_prefill_finish<<<1, 512, 0, st>>>(reinterpret_cast<const MaintDesc*>(e->maint_dev), K_all, V_all, q_len, nblk);
+    if ((s = check_launch("k_prefill_finish")) != TT_OK) return s;
+    e->h_total = q_len;
+    e->last_stream = st;
+    return TT_OK;
+}
+
+tt_status tt_engine_get_counters(tt_engine* e, tt_engine_counters* out) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (!out) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    DeviceGuard dg(e->cfg.device);
+    if ((s = check_cuda(cudaStreamSynchronize(e->last_stream), "engine sync")) != TT_OK) return s;
+    DevCounters c;
+    if ((s = check_cuda(cudaMemcpy(&c, e->ctr, sizeof(c), cudaMemcpyDeviceToHost), "counter read")) != TT_OK) return s;
+    if (c.error) return set_error((tt_status)c.error, "device-side engine error %d (packed capacity)", c.error);
+    out->s_count = c.s_count;
+    out->rw_count = c.rw_count;
+    out->rw_head_index = c.rw_head;
+    out->hh_count = c.hh_count;
+    out->wr_count = c.wr_count;
+    out->pbs_allocated_blocks = c.pbs_alloc;
+    out->pbs_blocks_used = c.pbs_used;
+    out->pbs_count = c.pbs_count;
+    out->total_processed_tokens = c.total;
+    out->total_evictions = c.total_evictions;
+    out->last_calc_pos = c.last_calc_pos;
+    out->max_hh = e->max_hh;
+    out->chunk_size = e->chunk;
+    out->cached_threshold = c.cached_threshold;
+    return TT_OK;
+}
+
+tt_status tt_engine_set_counters(tt_engine* e, const tt_engine_counters* in, void* stream) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (!in) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    const tt_engine_counters& c = *in;
+    if (c.s_count < 0 || c.s_count > e->cfg.sink_size || c.rw_count < 0 || c.rw_count > e->cfg.rw_size ||
+        c.rw_head_index < 0 || c.rw_head_index >= e->cfg.rw_size || c.hh_count < 0 || c.hh_count > e->max_hh ||
+        c.wr_count < 0 || c.wr_count >= e->chunk || c.pbs_blocks_used < 0 ||
+        c.pbs_allocated_blocks < c.pbs_blocks_used || c.pbs_count != c.pbs_blocks_used * e->chunk ||
+        c.total_processed_tokens < 0)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "inconsistent engine counters.");
+    DeviceGuard dg(e->cfg.device);
+    if (std::max(c.pbs_blocks_used + 1 + kLogicalSlack, c.pbs_allocated_blocks) > e->pbs_cap) {
+        if ((s = grow_pbs(e, std::max(c.pbs_blocks_used + 1 + kLogicalSlack, c.pbs_allocated_blocks))) != TT_OK)
+            return s;
+    }
+    DevCounters d;
+    memset(&d, 0, sizeof(d));
+    d.s_count = c.s_count; d.rw_count = c.rw_count; d.rw_head = c.rw_head_index; d.hh_count = c.hh_count;
+    d.wr_count = c.wr_count; d.pbs_alloc = c.pbs_allocated_blocks; d.pbs_used = c.pbs_blocks_used;
+    d.pbs_count = c.pbs_count; d.total = c.total_processed_tokens; d.total_evictions = c.total_evictions;
+    d.last_calc_pos = c.last_calc_pos; d.cached_threshold = c.cached_threshold;
+    cudaStream_t st = (cudaStream_t)stream;
+    if ((s = check_cuda(cudaMemcpyAsync(e->ctr, &d, sizeof(d), cudaMemcpyHostToDevice, st), "set counters")) != TT_OK)
+        return s;
+    if ((s = check_cuda(cudaStreamSynchronize(st), "set counters")) != TT_OK) return s;
+    e->h_total = c.total_processed_tokens;
+    e->h_s = c.s_count;
+    e->h_rw = c.rw_count;
+    e->h_rw_head = c.rw_head_index;
+    e->h_evictions = c.total_evictions;
+    e->h_wr_pbs_ub = (long long)c.pbs_count + c.wr_count;
+    e->last_stream = st;
+    return TT_OK;
+}
+
+tt_status tt_engine_get_buffer(tt_engine* e, int which, tt_buffer_desc* out) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (!out) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_engine_counters c;
+    if ((s = tt_engine_get_counters(e, &c)) != TT_OK) return s;
+    const size_t kvs = e->kvs, nb = (size_t)c.pbs_allocated_blocks, C = e->chunk;
+    const int m16 = e->cfg.meta_fp16;
+    const int mdt = m16 ? 3 : 0, mes = m16 ? 2 : 4;
+    auto set = [&](void* p, size_t n, int es, int dt) {
+        out->data = p; out->count = n; out->elem_size = es; out->dtype = dt;
+        return TT_OK;
+    };
+    switch (which) {
+        case TT_BUF_S_K: return set(e->S_K, (size_t)e->cfg.sink_size * kvs, 4, 0);
+        case TT_BUF_S_V: return set(e->S_V, (size_t)e->cfg.sink_size * kvs, 4, 0);
+        case TT_BUF_RW_K: return set(e->RW_K, (size_t)e->cfg.rw_size * kvs, 4, 0);
+        case TT_BUF_RW_V: return set(e->RW_V, (size_t)e->cfg.rw_size * kvs, 4, 0);
+        case TT_BUF_HH_K: return set(e->HH_K, (size_t)e->max_hh * kvs, 4, 0);
+        case TT_BUF_HH_V: return set(e->HH_V, (size_t)e->max_hh * kvs, 4, 0);
+        case TT_BUF_HH_TOKEN_IDS: return set(e->HH_ids, (size_t)e->max_hh, 8, 2);
+        case TT_BUF_HH_SCORES: return set(e->HH_scores, (size_t)e->max_hh, 4, 0);
+        case TT_BUF_WR_K: return set(e->WR_K, C * kvs, 4, 0);
+        case TT_BUF_WR_V: return set(e->WR_V, C * kvs, 4, 0);
+        case TT_BUF_WR_TOKEN_IDS: return set(e->WR_ids, C, 8, 2);
+        case TT_BUF_PBS_K_PACKED: return set(e->kp, nb * (C / 16) * kvs, 4, 1);
+        case TT_BUF_PBS_K_SCALES: return set(e->ks, nb * kvs, mes, mdt);
+        case TT_BUF_PBS_K_ZEROES: return set(e->kz, nb * kvs, mes, mdt);
+        case TT_BUF_PBS_V_PACKED: return set(e->vp, nb * C * e->cfg.num_kv_heads * e->qhd, 4, 1);
+        case TT_BUF_PBS_V_SCALES: return set(e->vs, nb * C * e->cfg.num_kv_heads, mes, mdt);
+        case TT_BUF_PBS_V_ZEROES: return set(e->vz, nb * C * e->cfg.num_kv_heads, mes, mdt);
+        case TT_BUF_PBS_TOKEN_IDS: return set(e->PBS_ids, nb * C, 8, 2);
+        case TT_BUF_GLOBAL_ATTN_SCORES: return set(e->g, (size_t)e->cfg.max_seq_len, 4, 0);
+    }
+    return set_error(TT_ERR_OUT_OF_RANGE, "unknown buffer id %d", which);
+}
+
+tt_status tt_engine_get_buffer_bytes(tt_engine* e, size_t* out) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    tt_engine_counters c;
+    if ((s = tt_engine_get_counters(e, &c)) != TT_OK) return s;
+    // cache_engine.cpp:543-568 over the reference's logical sizes
+    const size_t kvs = e->kvs, nb = (size_t)c.pbs_allocated_blocks, C = e->chunk, mb = e->meta_bytes;
+    size_t b = 0;
+    b += 2 * (size_t)e->cfg.sink_size * kvs * 4 + 2 * (size_t)e->cfg.rw_size * kvs * 4;
+    b += 2 * (size_t)e->max_hh * kvs * 4 + (size_t)e->max_hh * 8 + (size_t)e->max_hh * 4;
+    b += 2 * C * kvs * 4 + C * 8;
+    b += nb * (C / 16) * kvs * 4;
+    b += 2 * nb * kvs * mb + 2 * nb * C * e->cfg.num_kv_heads * mb;
+    b += nb * C * e->cfg.num_kv_heads * e->qhd * 4 + nb * C * 8;
+    b += (size_t)e->cfg.max_seq_len * 4;
+    *out = b;
+    return TT_OK;
+}
+
+tt_status tt_engine_device_bytes(tt_engine* e, size_t* out) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    const size_t kvs = e->kvs, nb = (size_t)e->pbs_cap, C = e->chunk, mb = e->meta_bytes;
+    size_t b = 0;
+    b += 2 * (size_t)std::max(e->cfg.sink_size, 1) * kvs * 4 + 2 * (size_t)e->cfg.rw_size * kvs * 4;
+    b += 2 * (size_t)e->max_hh * kvs * 4 + (size_t)e->max_hh * 12 + 2 * C * kvs * 4 + C * 8;
+    b += nb * (C / 16) * kvs * 4 + 2 * nb * kvs * mb + 2 * nb * C * e->cfg.num_kv_heads * mb;
+    b += nb * C * e->cfg.num_kv_heads * e->qhd * 4 + nb * C * 8 + (size_t)e->cfg.max_seq_len * 4;
+    b += e->scratch_floats * 4 + sizeof(DevCounters) + sizeof(JobDesc) + sizeof(MaintDesc);
+    *out = b;
+    return TT_OK;
+}
+
+}  // extern "C"
