@@ -249,6 +249,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="fewer layers (profiling cases only; the metric is quoted on 32)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
@@ -256,7 +258,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    cfg = CFG2
+    cfg = dict(CFG2)
+    if args.layers:
+        cfg["layers"] = args.layers
+        cfg["name"] = CFG2["name"].replace("32 layers", f"{args.layers} layers")
 
     if args.impl == "reference":
         return reference_arm(args, cfg, rank, world)
