@@ -64,6 +64,11 @@ typedef struct {
 tt_status tt_profile_enable(int on);
 tt_status tt_profile_collect(tt_kernel_times* out);
 
+/* Synchronises the device and reports the first device-side error recorded by
+ * the library's kernels (a bounded wait that expired: TT_ERR_TIMEOUT), 0 if
+ * none; clear != 0 resets it.  No reference counterpart. */
+tt_status tt_device_error(int clear, int* out);
+
 /* ---------------------------------------------------------------------- */
 /* Stand-alone kernels                                                     */
 /* ---------------------------------------------------------------------- */

@@ -61,6 +61,7 @@ EXPORTS = [
     "tt_engine_destroy", "tt_engine_step", "tt_engine_step_batched", "tt_engine_prefill",
     "tt_engine_get_counters", "tt_engine_get_buffer", "tt_engine_get_buffer_bytes",
     "tt_engine_device_bytes", "tt_engine_set_counters", "tt_profile_enable", "tt_profile_collect",
+    "tt_device_error",
 ]
 
 _lib = None
@@ -93,6 +94,7 @@ def _declare(L):
     L.tt_engine_set_counters.argtypes = [vp, C.POINTER(EngineCounters), vp]
     L.tt_profile_enable.argtypes = [i]
     L.tt_profile_collect.argtypes = [C.POINTER(KernelTimes)]
+    L.tt_device_error.argtypes = [i, C.POINTER(i)]
     for name in EXPORTS:
         if name not in ("tt_last_error", "tt_version"):
             getattr(L, name).restype = C.c_int

@@ -26,428 +26,15 @@
 
 #include "tt_attn.cuh"
 
+#include "tt_partial.cuh"
+
 namespace tt {
-
-constexpr int NT = 256;
-constexpr int NW = NT / TT_WARP;
-constexpr float kLog2e = 1.4426950408889634f;
-
-template <int HD>
-struct HDT {
-    static constexpr int CPL = HD >= 32 ? HD / 32 : 1;  // channels per lane in PV
-    static constexpr int DQ = HD / 16;                  // packed V words per (token, head)
-};
-
-// 4 + code as a float, code = the 2-bit field of `w` at bit `bit` (rot = (21 - bit) & 31):
-// rotate the field to mantissa bits 21-22 and set the exponent of [4, 8).
-__device__ __forceinline__ float unpack_4pc(uint32_t w, int rot) {
-    return __uint_as_float((__funnelshift_l(w, w, rot) & 0x00600000u) | 0x40800000u);
-}
-
-struct WarpSmem {
-    uint32_t* kw;      // [2][HD]
-    float* qs;         // [2][HD][GM]
-    uint32_t* vw;      // [32][DQ]
-    float* ws;         // [32][GM]
-    const float** vrow;  // [32]
-};
-
-template <int HD, int GM>
-struct SmemPlan {
-    static constexpr int kw = 2 * HD * 4;
-    static constexpr int qs = 2 * HD * GM * 4;
-    static constexpr int vw = 32 * (HD / 16) * 4;
-    static constexpr int ws = 32 * GM * 4;
-    static constexpr int vrow = 32 * 8;
-    static constexpr int per_warp = kw + qs + vw + ws + vrow;
-    static constexpr int merge = NW * GM * (HD + 2) * 4;
-    static size_t bytes(int HG) {
-        size_t q = (size_t)HG * GM * HD * 4;
-        size_t body = (size_t)NW * per_warp;
-        if ((size_t)merge > body) body = merge;
-        return q + body;
-    }
-};
-
-__device__ __forceinline__ void dense_slot(const JobDesc& J, const TierCounts& tc, int i, const float*& Kb,
-                                           const float*& Vb, int& slot) {
-    if (i < tc.n0) {
-        Kb = J.K0; Vb = J.V0; slot = i;
-    } else if (i < tc.n0 + tc.n1) {
-        Kb = J.K1; Vb = J.V1; slot = i - tc.n0;
-    } else {
-        Kb = J.K2; Vb = J.V2;
-        const int r = i - tc.n0 - tc.n1;
-        slot = tc.ring_size > 0 ? (tc.ring_head + r) % tc.ring_size : r;
-    }
-}
-
-template <int HD, int GM>
-__global__ void __launch_bounds__(NT) k_attn_partial(const __grid_constant__ AttnLaunch L) {
-    using T = HDT<HD>;
-    using SP = SmemPlan<HD, GM>;
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ JobDesc Js;
-    __shared__ TierCounts Ts;
-
-    const int job = blockIdx.y / L.nhg;
-    const int hg = blockIdx.y - job * L.nhg;
-    if (threadIdx.x == 0) {
-        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
-        Ts = resolve_counts(Js);
-    }
-    __syncthreads();
-    const JobDesc& J = Js;
-    const TierCounts tc = Ts;
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const int ntok = tc.nblk * J.grp;
-    const bool is_dense = (int)blockIdx.x < L.nd;
-    int t0, t1;
-    if (is_dense) {
-        t0 = blockIdx.x * L.DC;
-        t1 = min(D, t0 + L.DC);
-    } else {
-        t0 = (blockIdx.x - L.nd) * L.PC;
-        t1 = min(ntok, t0 + L.PC);
-    }
-    if (t0 >= t1) return;
-
-    const int nq = J.nq, nkv = J.nkv, G = L.G, HG = L.HG;
-    const size_t kvs = (size_t)nkv * HD;
-    const float* __restrict__ Q = L.Q[job];
-
-    // ---- stage the query rows of this kv-head group: q_s[kvl][g][c] ----
-    float* q_s = reinterpret_cast<float*>(smem);
-    for (int i = threadIdx.x; i < HG * GM * HD; i += NT) {
-        const int c = i % HD, kg = i / HD, g = kg % GM, kvl = kg / GM;
-        q_s[i] = g < G ? Q[((size_t)(hg * HG + kvl) * G + g) * HD + c] : 0.f;
-    }
-    __syncthreads();
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kvl = warp % HG, r0 = warp / HG, WPH = NW / HG;
-    const int kvh = hg * HG + kvl;
-    unsigned char* wbase = smem + (size_t)HG * GM * HD * 4 + (size_t)warp * SP::per_warp;
-    WarpSmem W;
-    W.kw = reinterpret_cast<uint32_t*>(wbase);
-    W.qs = reinterpret_cast<float*>(wbase + SP::kw);
-    W.vw = reinterpret_cast<uint32_t*>(wbase + SP::kw + SP::qs);
-    W.ws = reinterpret_cast<float*>(wbase + SP::kw + SP::qs + SP::vw);
-    W.vrow = reinterpret_cast<const float**>(wbase + SP::kw + SP::qs + SP::vw + SP::ws);
-    const float* qk = q_s + (size_t)kvl * GM * HD;
-    const float sc = (1.0f / sqrtf((float)HD)) * kLog2e;  // log2-domain logit scale
-    const int meta16 = J.meta16;
-
-    float m[GM], l[GM], sws[GM], spz[GM];
-    float acc[GM][T::CPL];
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-        m[g] = -INFINITY; l[g] = 0.f; sws[g] = 0.f; spz[g] = 0.f;
-#pragma unroll
-        for (int j = 0; j < T::CPL; ++j) acc[g][j] = 0.f;
-    }
-
-    for (int u = r0; t0 + u * 32 < t1; u += WPH) {
-        const int ub = t0 + u * 32;
-        const int tk = ub + lane;
-        const bool inr = tk < t1;
-        const int nt = min(32, t1 - ub);
-        float s[GM];
-
-        if (is_dense) {
-            // ---------------- dense QK: lane <-> token ----------------
-            if (inr) {
-                const float *Kb, *Vb;
-                int slot;
-                dense_slot(J, tc, tk, Kb, Vb, slot);
-                const float4* krow = reinterpret_cast<const float4*>(Kb + (size_t)slot * kvs + (size_t)kvh * HD);
-                W.vrow[lane] = Vb + (size_t)slot * kvs + (size_t)kvh * HD;
-                float a[GM];
-#pragma unroll
-                for (int g = 0; g < GM; ++g) a[g] = 0.f;
-#pragma unroll 4
-                for (int c4 = 0; c4 < HD / 4; ++c4) {
-                    const float4 k = krow[c4];
-#pragma unroll
-                    for (int g = 0; g < GM; ++g) {
-                        const float4 q = reinterpret_cast<const float4*>(qk + g * HD)[c4];
-                        a[g] = fmaf(q.x, k.x, a[g]);
-                        a[g] = fmaf(q.y, k.y, a[g]);
-                        a[g] = fmaf(q.z, k.z, a[g]);
-                        a[g] = fmaf(q.w, k.w, a[g]);
-                    }
-                }
-#pragma unroll
-                for (int g = 0; g < GM; ++g) s[g] = a[g] * sc;
-            } else {
-#pragma unroll
-                for (int g = 0; g < GM; ++g) s[g] = -INFINITY;
-            }
-        } else {
-            // ---------------- PBS: stage words, q*scale, bias sums ----------------
-            float bs[2][GM], bz[2][GM];
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-                for (int g = 0; g < GM; ++g) { bs[hf][g] = 0.f; bz[hf][g] = 0.f; }
-                const int tb = ub + hf * 16;
-                if (tb < t1) {
-                    const int krow = tb >> 4, mrow = tb / J.grp;
-                    const uint32_t* kp = reinterpret_cast<const uint32_t*>(J.kp) + ((size_t)krow * nkv + kvh) * HD;
-                    const size_t mb = ((size_t)mrow * nkv + kvh) * HD;
-#pragma unroll
-                    for (int j = 0; j < T::CPL; ++j) {
-                        const int c = lane * T::CPL + j;
-                        if (c < HD) {
-                            W.kw[hf * HD + c] = __ldg(kp + c);
-                            const float sv = load_meta(J.ks, mb + c, meta16);
-                            const float zv = load_meta(J.kz, mb + c, meta16);
-#pragma unroll
-                            for (int g = 0; g < GM; ++g) {
-                                const float qv = qk[g * HD + c];
-                                const float v = qv * sv;
-                                W.qs[(hf * HD + c) * GM + g] = v;
-                                bs[hf][g] += v;
-                                bz[hf][g] = fmaf(qv, zv, bz[hf][g]);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int g = 0; g < GM; ++g) {
-                        bs[hf][g] = warp_sum(bs[hf][g]);
-                        bz[hf][g] = warp_sum(bz[hf][g]);
-                    }
-                }
-            }
-            __syncwarp();
-            // ---------------- PBS QK: lane <-> token ----------------
-            const int hf = lane >> 4;
-            const int rot = (21 - 2 * (lane & 15)) & 31;
-            float a[GM];
-#pragma unroll
-            for (int g = 0; g < GM; ++g) a[g] = 0.f;
-            if (inr) {
-                const uint4* kw4 = reinterpret_cast<const uint4*>(W.kw + hf * HD);
-                const float* qsh = W.qs + (size_t)hf * HD * GM;
-#pragma unroll 2
-                for (int c4 = 0; c4 < HD / 4; ++c4) {
-                    const uint4 w4 = kw4[c4];
-                    const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                    for (int jj = 0; jj < 4; ++jj) {
-                        const float F = unpack_4pc(ww[jj], rot);
-                        const float* qc = qsh + (c4 * 4 + jj) * GM;
-                        if constexpr (GM % 4 == 0) {
-#pragma unroll
-                            for (int g4 = 0; g4 < GM / 4; ++g4) {
-                                const float4 qv = reinterpret_cast<const float4*>(qc)[g4];
-                                a[g4 * 4 + 0] = fmaf(qv.x, F, a[g4 * 4 + 0]);
-                                a[g4 * 4 + 1] = fmaf(qv.y, F, a[g4 * 4 + 1]);
-                                a[g4 * 4 + 2] = fmaf(qv.z, F, a[g4 * 4 + 2]);
-                                a[g4 * 4 + 3] = fmaf(qv.w, F, a[g4 * 4 + 3]);
-                            }
-                        } else {
-#pragma unroll
-                            for (int g = 0; g < GM; ++g) a[g] = fmaf(qc[g], F, a[g]);
-                        }
-                    }
-                }
-            }
-            const bool live = inr && J.ids[tk] != -1;
-#pragma unroll
-            for (int g = 0; g < GM; ++g) {
-                const float bsg = hf ? bs[1][g] : bs[0][g];
-                const float bzg = hf ? bz[1][g] : bz[0][g];
-                s[g] = live ? ((a[g] - 4.0f * bsg) + bzg) * sc : -INFINITY;
-            }
-        }
-
-        // ---------------- logits to scratch (mean weights) ----------------
-        if (inr) {
-            const int pos = is_dense ? tk : D + tk;
-#pragma unroll
-            for (int g = 0; g < GM; ++g)
-                if (g < G) J.scores[(size_t)(kvh * G + g) * J.score_stride + pos] = s[g];
-        }
-
-        // ---------------- online softmax ----------------
-        float vsc = 0.f, vzr = 0.f;
-        if (!is_dense && inr) {
-            const size_t mi = (size_t)tk * nkv + kvh;
-            vsc = load_meta(J.vs, mi, meta16);
-            vzr = load_meta(J.vz, mi, meta16);
-        }
-#pragma unroll
-        for (int g = 0; g < GM; ++g) {
-            const float mu = warp_max(s[g]);
-            const float mn = fmaxf(m[g], mu);
-            float alpha = 1.f, p = 0.f;
-            if (mn != -INFINITY) {
-                alpha = exp2f(m[g] - mn);
-                p = s[g] == -INFINITY ? 0.f : exp2f(s[g] - mn);
-            }
-            m[g] = mn;
-            l[g] = fmaf(l[g], alpha, p);
-            sws[g] *= alpha;
-            spz[g] *= alpha;
-#pragma unroll
-            for (int j = 0; j < T::CPL; ++j) acc[g][j] *= alpha;
-            if (is_dense) {
-                W.ws[lane * GM + g] = p;
-            } else {
-                const float wsv = p * vsc;
-                sws[g] += wsv;
-                spz[g] = fmaf(p, vzr, spz[g]);
-                W.ws[lane * GM + g] = wsv;
-            }
-        }
-
-        // ---------------- PV: lane <-> channels ----------------
-        if (is_dense) {
-            __syncwarp();
-            for (int t = 0; t < nt; ++t) {
-                const float* vr = W.vrow[t] + lane * T::CPL;
-                float v[T::CPL];
-                if constexpr (T::CPL == 4) {
-                    const float4 x = ldg_stream_f4(vr);
-                    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-                } else if constexpr (T::CPL == 8) {
-                    const float4 x = ldg_stream_f4(vr), y = ldg_stream_f4(vr + 4);
-                    v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
-                    v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
-                } else {
-#pragma unroll
-                    for (int j = 0; j < T::CPL; ++j) v[j] = (lane * T::CPL + j < HD) ? __ldg(vr + j) : 0.f;
-                }
-#pragma unroll
-                for (int g = 0; g < GM; ++g) {
-                    const float p = W.ws[t * GM + g];
-#pragma unroll
-                    for (int j = 0; j < T::CPL; ++j) acc[g][j] = fmaf(p, v[j], acc[g][j]);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < T::DQ; ++i) {
-                const int idx = i * 32 + lane;
-                const int t = idx / T::DQ, wi = idx - (idx / T::DQ) * T::DQ;
-                const int tok = ub + t;
-                W.vw[t * T::DQ + wi] =
-                    tok < t1 ? __ldg(reinterpret_cast<const uint32_t*>(J.vp) + ((size_t)tok * nkv + kvh) * T::DQ + wi) : 0u;
-            }
-            __syncwarp();
-            const int wsel = min(lane * T::CPL, HD - 1) / 16;
-            for (int t = 0; t < nt; ++t) {
-                const uint32_t w = W.vw[t * T::DQ + wsel];
-                float wg[GM];
-                if constexpr (GM % 4 == 0) {
-#pragma unroll
-                    for (int g4 = 0; g4 < GM / 4; ++g4) {
-                        const float4 x = reinterpret_cast<const float4*>(W.ws + t * GM)[g4];
-                        wg[g4 * 4 + 0] = x.x; wg[g4 * 4 + 1] = x.y; wg[g4 * 4 + 2] = x.z; wg[g4 * 4 + 3] = x.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int g = 0; g < GM; ++g) wg[g] = W.ws[t * GM + g];
-                }
-#pragma unroll
-                for (int j = 0; j < T::CPL; ++j) {
-                    const int bit = 2 * ((lane * T::CPL + j) & 15);
-                    const float F = unpack_4pc(w, (21 - bit) & 31);
-#pragma unroll
-                    for (int g = 0; g < GM; ++g) acc[g][j] = fmaf(wg[g], F, acc[g][j]);
-                }
-            }
-        }
-        __syncwarp();
-    }
-
-    // ---- per-warp totals: l, and for packed V the bias terms ----
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-        l[g] = warp_sum(l[g]);
-        if (!is_dense) {
-            const float SW = warp_sum(sws[g]);
-            const float SZ = warp_sum(spz[g]);
-#pragma unroll
-            for (int j = 0; j < T::CPL; ++j) acc[g][j] = (acc[g][j] - 4.0f * SW) + SZ;
-        }
-    }
-
-    const int chunk = blockIdx.x;
-    if (WPH == 1) {
-#pragma unroll
-        for (int g = 0; g < GM; ++g) {
-            if (g >= G) break;
-            const size_t qh = (size_t)kvh * G + g;
-            const size_t pi = (size_t)chunk * nq + qh;
-            if (lane == 0) {
-                J.part_ml[pi * 2 + 0] = m[g];
-                J.part_ml[pi * 2 + 1] = l[g];
-            }
-#pragma unroll
-            for (int j = 0; j < T::CPL; ++j) {
-                const int c = lane * T::CPL + j;
-                if (c < HD) J.part_acc[pi * HD + c] = acc[g][j];
-            }
-        }
-        return;
-    }
-    // ---- merge the WPH warps that share a kv head ----
-    __syncthreads();
-    float* mb = reinterpret_cast<float*>(smem + (size_t)HG * GM * HD * 4);
-    float* mine = mb + (size_t)warp * GM * (HD + 2);
-#pragma unroll
-    for (int g = 0; g < GM; ++g) {
-        if (lane == 0) {
-            mine[g * (HD + 2) + 0] = m[g];
-            mine[g * (HD + 2) + 1] = l[g];
-        }
-#pragma unroll
-        for (int j = 0; j < T::CPL; ++j) {
-            const int c = lane * T::CPL + j;
-            if (c < HD) mine[g * (HD + 2) + 2 + c] = acc[g][j];
-        }
-    }
-    __syncthreads();
-    if (r0 != 0) return;
-    for (int g = 0; g < G && g < GM; ++g) {
-        float M = -INFINITY;
-        for (int r = 0; r < WPH; ++r) M = fmaxf(M, mb[(size_t)(r * HG + kvl) * GM * (HD + 2) + g * (HD + 2)]);
-        float Ls = 0.f;
-        float o[T::CPL];
-#pragma unroll
-        for (int j = 0; j < T::CPL; ++j) o[j] = 0.f;
-        for (int r = 0; r < WPH; ++r) {
-            const float* src = mb + (size_t)(r * HG + kvl) * GM * (HD + 2) + g * (HD + 2);
-            const float mr = src[0];
-            if (mr == -INFINITY) continue;
-            const float f = exp2f(mr - M);
-            Ls = fmaf(src[1], f, Ls);
-#pragma unroll
-            for (int j = 0; j < T::CPL; ++j) {
-                const int c = lane * T::CPL + j;
-                if (c < HD) o[j] = fmaf(src[2 + c], f, o[j]);
-            }
-        }
-        const size_t pi = (size_t)chunk * nq + (size_t)kvh * G + g;
-        if (lane == 0) {
-            J.part_ml[pi * 2 + 0] = M;
-            J.part_ml[pi * 2 + 1] = Ls;
-        }
-#pragma unroll
-        for (int j = 0; j < T::CPL; ++j) {
-            const int c = lane * T::CPL + j;
-            if (c < HD) J.part_acc[pi * HD + c] = o[j];
-        }
-    }
-}
 
 // ---------------------------------------------------------------------------
 // merge + mean weights + score feedback
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ AttnLaunch L) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y;
@@ -464,59 +51,82 @@ __global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ At
     const int T = D + ntok;
     const int nd_act = ceil_div(D, L.DC), np_act = ceil_div(ntok, L.PC);
     const int nch = nd_act + np_act;
-    float* Ms = reinterpret_cast<float*>(smem);
-    float* Ls = Ms + nq;
+    float* Ms = reinterpret_cast<float*>(smem);   // [nq]
+    float* IL = Ms + nq;                          // [nq] 1 / L
+    float* wts = IL + nq;                         // [nch] merge weights of one head
+    float* red = wts + nch;                       // [NT] partial output sums
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto chunk_index = [&](int i) { return i < nd_act ? i : L.nd + (i - nd_act); };
 
+    // ---- global (M, L) per head from the chunk partials ----
     for (int h = warp; h < nq; h += NW) {
         float M = -INFINITY;
-        for (int i = lane; i < nch; i += 32) {
-            const int ci = i < nd_act ? i : L.nd + (i - nd_act);
-            M = fmaxf(M, J.part_ml[((size_t)ci * nq + h) * 2]);
-        }
+        for (int i = lane; i < nch; i += 32) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
         M = warp_max(M);
         float S = 0.f;
         if (M != -INFINITY) {
             for (int i = lane; i < nch; i += 32) {
-                const int ci = i < nd_act ? i : L.nd + (i - nd_act);
-                const float mi = J.part_ml[((size_t)ci * nq + h) * 2];
-                if (mi != -INFINITY) S = fmaf(J.part_ml[((size_t)ci * nq + h) * 2 + 1], exp2f(mi - M), S);
+                const size_t pi = ((size_t)chunk_index(i) * nq + h) * 2;
+                const float mi = J.part_ml[pi];
+                if (mi != -INFINITY) S = fmaf(J.part_ml[pi + 1], exp2f(mi - M), S);
             }
         }
         S = warp_sum(S);
         if (lane == 0) {
             Ms[h] = M;
-            Ls[h] = S > 0.f ? S : 1.0f;  // row_sum_exp fallback (fused_attn_avx2.cpp:261)
+            IL[h] = 1.0f / (S > 0.f ? S : 1.0f);  // row_sum_exp fallback (fused_attn_avx2.cpp:261)
         }
     }
     __syncthreads();
 
     // ---- attention output: heads blockIdx.x, blockIdx.x + nfin, ... ----
     float* out = L.out[job];
+    const int groups = NT / HD > 0 ? NT / HD : 1;  // threads per channel
     for (int h = blockIdx.x; h < nq; h += L.nfin) {
-        const float M = Ms[h], inv = 1.0f / Ls[h];
-        for (int c = threadIdx.x; c < HD; c += NT) {
+        const float M = Ms[h], inv = IL[h];
+        for (int i = threadIdx.x; i < nch; i += NT) {
+            const float mi = J.part_ml[((size_t)chunk_index(i) * nq + h) * 2];
+            wts[i] = (M == -INFINITY || mi == -INFINITY) ? 0.f : exp2f(mi - M) * inv;
+        }
+        __syncthreads();
+        for (int c0 = 0; c0 < HD; c0 += NT) {
+            const int c = c0 + (threadIdx.x % HD), grp_i = threadIdx.x / HD;
             float o = 0.f;
-            if (M != -INFINITY) {
-                for (int i = 0; i < nch; ++i) {
-                    const int ci = i < nd_act ? i : L.nd + (i - nd_act);
-                    const float mi = J.part_ml[((size_t)ci * nq + h) * 2];
-                    if (mi == -INFINITY) continue;
-                    o = fmaf(J.part_acc[((size_t)ci * nq + h) * HD + c], exp2f(mi - M), o);
-                }
+            if (c < HD && grp_i < groups) {
+#pragma unroll 4
+                for (int i = grp_i; i < nch; i += groups)
+                    o = fmaf(J.part_acc[((size_t)chunk_index(i) * nq + h) * HD + c], wts[i], o);
             }
-            out[(size_t)h * HD + c] = o * inv;
+            red[threadIdx.x] = o;
+            __syncthreads();
+            if (threadIdx.x < HD && c0 + threadIdx.x < HD) {
+                float t = 0.f;
+                for (int k = 0; k < groups; ++k) t += red[k * HD + threadIdx.x];
+                out[(size_t)h * HD + c0 + threadIdx.x] = t;
+            }
+            __syncthreads();
         }
     }
 
     // ---- mean attention weights over heads, score feedback ----
     float* mw = L.mw[job];
     const int p0 = blockIdx.x * L.FT, p1 = min(T, p0 + L.FT);
+    const float* sc = J.scores;
+    const size_t stride = (size_t)J.score_stride;
     for (int pos = p0 + threadIdx.x; pos < p1; pos += NT) {
         float sw = 0.f;
-        for (int h = 0; h < nq; ++h) {
-            const float s = J.scores[(size_t)h * J.score_stride + pos];
-            if (s != -INFINITY) sw += exp2f(s - Ms[h]) / Ls[h];
+        int h = 0;
+        for (; h + 8 <= nq; h += 8) {
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (v[k] != -INFINITY) sw = fmaf(exp2f(v[k] - Ms[h + k]), IL[h + k], sw);
+        }
+        for (; h < nq; ++h) {
+            const float v = sc[(size_t)h * stride + pos];
+            if (v != -INFINITY) sw = fmaf(exp2f(v - Ms[h]), IL[h], sw);
         }
         const float w = sw / (float)nq;
         if (mw) mw[pos] = w;
@@ -546,7 +156,7 @@ __global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ At
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-int attn_max_chunks(int dense_cap, int pbs_tok_cap) { return ceil_div(dense_cap, 64) + ceil_div(pbs_tok_cap, 64) + 2; }
+int attn_max_chunks(int dense_cap, int pbs_tok_cap) { return ceil_div(dense_cap, 32) + ceil_div(pbs_tok_cap, 64) + 2; }
 
 static int pick_gm(int G) {
     if (G <= 1) return 1;
@@ -562,15 +172,28 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
     if (!pick_gm(L.G)) return set_error(TT_ERR_UNSUPPORTED, "more than 8 query heads per kv head is not supported.");
     if (hd != 16 && hd != 32 && hd != 64 && hd != 128 && hd != 256)
         return set_error(TT_ERR_UNSUPPORTED, "head_dim %d not supported (16, 32, 64, 128, 256).", hd);
-    L.HG = (nkv % 8 == 0) ? 8 : (nkv % 4 == 0) ? 4 : (nkv % 2 == 0) ? 2 : 1;
+    // A kv-head group is staged as one contiguous run per region when it holds
+    // every kv head (nkv <= 8); wider models split into groups of 8.
+    if (nkv <= 8) {
+        L.HG = nkv;
+    } else if (nkv % 8 == 0) {
+        L.HG = 8;
+    } else {
+        return set_error(TT_ERR_UNSUPPORTED, "num_kv_heads > 8 must be a multiple of 8 (got %d).", nkv);
+    }
     L.nhg = nkv / L.HG;
-    // Aim for about four resident CTAs' worth of work per SM across the launch.
-    const long long work = (long long)L.njobs * L.nhg * ((long long)dense_cap + pbs_tok_cap);
-    long long cs = work / (4LL * 148);
-    cs = (cs + 31) / 32 * 32;
-    cs = std::max(64LL, std::min(2048LL, cs));
-    L.DC = (int)cs;
-    L.PC = (int)cs;
+    // Chunks are sized by bytes: a dense FP32 token moves ~10x the bytes of a
+    // packed one.  Aim for about four CTAs of work per SM over the launch.
+    const double dense_tok = (double)L.HG * hd * 8.0;
+    const double pbs_tok = (double)L.HG * (hd / 2.0 + 2.0 * hd * 4 / 16.0 + 8.0) + 8.0;
+    const double total = (double)L.njobs * L.nhg * (dense_cap * dense_tok + pbs_tok_cap * pbs_tok);
+    const double per_cta = std::max(total / (4.0 * 148.0), 1.0);
+    auto tokens = [](double t, long long lo, long long hi) {
+        long long c = ((long long)t + 31) / 32 * 32;
+        return (int)std::max(lo, std::min(hi, c));
+    };
+    L.DC = tokens(per_cta / dense_tok, 32, 1024);
+    L.PC = tokens(per_cta / pbs_tok, 64, 4096);
     L.nd = ceil_div(dense_cap, L.DC);
     L.np = ceil_div(pbs_tok_cap, L.PC);
     L.FT = 1024;
@@ -580,13 +203,15 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
 
 template <int HD, int GM>
 static tt_status launch_partial_t(const AttnLaunch& L, cudaStream_t st) {
-    const size_t sm = SmemPlan<HD, GM>::bytes(L.HG);
+    const size_t sm = partial_smem_bytes<HD, GM>(L.HG, L.meta_bytes);
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
+        size_t mx = 0;
+        for (int hg = 1; hg <= 8; hg *= 2) mx = std::max(mx, partial_smem_bytes<HD, GM>(hg, 4));
         cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)SmemPlan<HD, GM>::bytes(8));
+                                             (int)mx);
         if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(k_attn_partial)");
         configured[dev & 63] = true;
     }
@@ -627,7 +252,8 @@ tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
     }
     dim3 grid(L.nfin, L.njobs);
     const int ps = prof_begin(2, st);
-    k_attn_finalize<<<grid, NT, (size_t)2 * L.inline_job.nq * sizeof(float), st>>>(L);
+    const size_t fsm = ((size_t)2 * L.inline_job.nq + (size_t)(L.nd + L.np) + NT) * sizeof(float);
+    k_attn_finalize<<<grid, NT, fsm, st>>>(L);
     prof_end(ps, st);
     return check_launch("k_attn_finalize");
 }
@@ -662,6 +288,19 @@ static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 using namespace tt;
 
+extern "C" tt_status tt_device_error(int clear, int* out) {
+    if (!out) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_status s = check_cuda(cudaDeviceSynchronize(), "tt_device_error");
+    if (s != TT_OK) return s;
+    s = check_cuda(cudaMemcpyFromSymbol(out, g_device_error, sizeof(int)), "tt_device_error");
+    if (s != TT_OK) return s;
+    if (clear) {
+        const int zero = 0;
+        s = check_cuda(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int)), "tt_device_error");
+    }
+    return s;
+}
+
 extern "C" tt_status tt_fused_attention_decode(const float* Q, const float* dense_K, const float* dense_V,
                                                int dense_count, const int32_t* PBS_K_Packed,
                                                const void* PBS_K_Scales, const void* PBS_K_Zeroes,
@@ -685,8 +324,10 @@ extern "C" tt_status tt_fused_attention_decode(const float* Q, const float* dens
     if (num_blocks > 0 && head_dim % 16 != 0)
         return set_error(TT_ERR_UNSUPPORTED, "head_dim must be a multiple of 16 for packed V rows.");
     if (!aligned16(Q) || (dense_count > 0 && (!aligned16(dense_K) || !aligned16(dense_V))) ||
-        (num_blocks > 0 && (!aligned16(PBS_K_Packed) || !aligned16(PBS_V_Packed))))
-        return set_error(TT_ERR_INVALID_ARGUMENT, "Q, dense_K, dense_V and packed PBS buffers must be 16-byte aligned.");
+        (num_blocks > 0 && (!aligned16(PBS_K_Packed) || !aligned16(PBS_V_Packed) || !aligned16(PBS_K_Scales) ||
+                            !aligned16(PBS_K_Zeroes) || !aligned16(PBS_V_Scales) || !aligned16(PBS_V_Zeroes) ||
+                            !aligned16(PBS_token_ids))))
+        return set_error(TT_ERR_INVALID_ARGUMENT, "Q, dense_K, dense_V and the PBS buffers must be 16-byte aligned.");
 
     AttnLaunch L;
     memset(&L, 0, sizeof(L));
@@ -719,6 +360,7 @@ extern "C" tt_status tt_fused_attention_decode(const float* Q, const float* dens
     J.max_chunks = maxch;
     J.g = nullptr; J.hh_scores = nullptr; J.hh_ids = nullptr; J.decay = 0.f; J.msl = 0;
     L.jobs[0] = nullptr;
+    L.meta_bytes = meta_fp16 ? 2 : 4;
     L.Q[0] = Q;
     L.out[0] = attn_output;
     L.mw[0] = mean_attn_weights;

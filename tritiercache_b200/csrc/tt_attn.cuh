@@ -87,6 +87,7 @@ struct AttnLaunch {
     int PC;       // PBS tokens per chunk (multiple of 32)
     int FT;       // tokens per finalize CTA
     int nfin;     // finalize CTAs per job
+    int meta_bytes;  // largest PBS metadata element of the batch (2 or 4): sizes the staging buffers
     const JobDesc* jobs[kMaxBatch];  // device descriptor per job (engines) or nullptr
     JobDesc inline_job;              // stand-alone job (jobs[0] == nullptr, njobs == 1)
     const float* Q[kMaxBatch];

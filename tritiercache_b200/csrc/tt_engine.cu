@@ -654,6 +654,9 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
         if (s != TT_OK) return s;
         L.inline_job.hd = c0.head_dim;
         L.inline_job.nq = c0.num_q_heads;
+        L.meta_bytes = 2;
+        for (int i = 0; i < m; ++i)
+            if (!engines[base + i]->cfg.meta_fp16) L.meta_bytes = 4;
         for (int i = 0; i < m; ++i) {
             tt_engine* e = engines[base + i];
             L.jobs[i] = e->job_dev;

@@ -1,0 +1,811 @@
+// tt_partial.cuh -- k_attn_partial: split-KV decode attention over one chunk
+// of dense (FP32) or packed (2-bit) tokens for one kv-head group.  Included by
+// tt_attn.cu only.
+//
+// Packed chunks stream through shared memory in stages of 256 (token, kv-head)
+// pairs with 1-D TMA bulk copies (cp.async.bulk ... mbarrier::complete_tx),
+// two stages in flight.  Every mbarrier wait is bounded: on expiry the CTA
+// records TT_ERR_TIMEOUT in the device error word, drains its own copies
+// (again bounded) and returns.  No multicast and no cluster launch.
+//
+// Per 32-token unit and kv head (one warp):
+//   QK lane <-> token:  score = sum_c qs_c*(4+code) - 4*sum qs + sum q*zero,
+//       qs = q*scale per block and channel (tabled in shared memory), the
+//       2-bit code rotated into a float's mantissa (unpack_4pc), two query
+//       heads per packed f32x2 FMA.
+//   PV lane <-> channels: acc += (p*vscale) * (4+code), two channels per
+//       f32x2 FMA; the running sums of p*vscale and p*vzero fold the
+//       zero/offset back in at the end.
+#pragma once
+#include "tt_attn.cuh"
+
+namespace tt {
+
+constexpr int NT = 256;
+constexpr int NW = NT / TT_WARP;
+constexpr int NSTAGE = 2;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ int g_device_error = 0;  // first device-side error code (tt_status), cleared by the host
+
+template <int HD>
+struct HDT {
+    static constexpr int CPL = HD >= 32 ? HD / 32 : 1;  // channels per lane in PV
+    static constexpr int DQ = HD / 16;                  // packed V words per (token, head)
+};
+
+// ---------------------------------------------------------------------------
+// small PTX helpers
+// ---------------------------------------------------------------------------
+typedef unsigned long long u64;
+
+__device__ __forceinline__ u64 f2pack(float lo, float hi) {
+    u64 r;
+    asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2unpack(u64 r) {
+    float2 v;
+    asm("mov.b64 {%0,%1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+    return v;
+}
+__device__ __forceinline__ u64 ffma2(u64 a, u64 b, u64 c) {
+    u64 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ u64 fmul2(u64 a, u64 b) {
+    u64 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float warp_max_redux(float v) {
+    float m;
+    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(m) : "f"(v));
+    return m;
+}
+
+// 4 + code as a float, code = the 2-bit field of `w` at bit `bit` (rot = (21 - bit) & 31):
+// rotate the field to mantissa bits 21-22 and set the exponent of [4, 8).
+__device__ __forceinline__ float unpack_4pc(uint32_t w, int rot) {
+    return __uint_as_float((__funnelshift_l(w, w, rot) & 0x00600000u) | 0x40800000u);
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait: about 2^20 polls (each try_wait may itself suspend briefly).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+    for (int i = 0; i < (1 << 20); ++i)
+        if (mbar_try_wait(bar, phase)) return true;
+    return false;
+}
+// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory plan
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// One stage holds ST = 32 * (NW / HG) tokens of the HG heads of a group
+// (at most 256 (token, kv head) pairs).
+__host__ __device__ __forceinline__ int stage_tokens(int HG) { return 32 * (NW / HG); }
+
+struct StageLayout {
+    int kw, ks, kz, vw, vs, vz, ids, bytes;
+};
+__host__ __device__ __forceinline__ StageLayout stage_layout(int HD, int mb) {
+    StageLayout s;
+    int o = 0;
+    s.kw = o; o += 16 * HD * 4;              // [ST/16 rows][HG][HD] words   (rows*HG = 16)
+    s.ks = o; o += align_up(16 * HD * mb, 16);  // [blocks][HG][HD]        (blocks*HG <= 16)
+    s.kz = o; o += align_up(16 * HD * mb, 16);
+    s.vw = o; o += 256 * (HD / 16) * 4;      // [ST][HG][DQ]
+    s.vs = o; o += align_up(256 * mb, 16);   // [ST][HG]
+    s.vz = o; o += align_up(256 * mb, 16);
+    s.ids = o; o += 256 * 8;                 // [ST] (ST <= 256)
+    s.bytes = align_up(o, 128);
+    return s;
+}
+
+template <int HD, int GM>
+struct WarpArea {
+    // packed units: q*scale table [half][HD][GM]; dense units reuse the same
+    // bytes for the logits transpose [token][GM] and the V row pointers
+    static constexpr int qs_packed = 2 * HD * GM * 4;
+    static constexpr int qs_dense = 32 * GM * 4 + 32 * 8;
+    static constexpr int qs = qs_packed > qs_dense ? qs_packed : qs_dense;
+    static constexpr int ws = 32 * GM * 8;      // [token][GM] (w, w) pairs
+    static constexpr int bias = 2 * 2 * GM * 4; // [half][sum qs | sum q*z][GM]
+    static constexpr int sc = 0;
+    static constexpr int vrow = 32 * GM * 4;
+    static constexpr int bytes = qs + ws + bias;
+};
+
+template <int HD, int GM>
+__host__ __device__ __forceinline__ size_t partial_smem_bytes(int HG, int mb) {
+    const size_t q = (size_t)align_up(HG * GM * HD * 4, 128);
+    const size_t body = (size_t)NSTAGE * stage_layout(HD, mb).bytes + (size_t)NW * WarpArea<HD, GM>::bytes;
+    const size_t merge = (size_t)NW * GM * (HD + 2) * 4;
+    return q + (body > merge ? body : merge);
+}
+
+__device__ __forceinline__ void dense_slot(const JobDesc& J, const TierCounts& tc, int i, const float*& Kb,
+                                           const float*& Vb, int& slot) {
+    if (i < tc.n0) {
+        Kb = J.K0; Vb = J.V0; slot = i;
+    } else if (i < tc.n0 + tc.n1) {
+        Kb = J.K1; Vb = J.V1; slot = i - tc.n0;
+    } else {
+        Kb = J.K2; Vb = J.V2;
+        const int r = i - tc.n0 - tc.n1;
+        slot = tc.ring_size > 0 ? (tc.ring_head + r) % tc.ring_size : r;
+    }
+}
+
+// Per-warp online-softmax state.  acc holds channel pairs (lane owns CPL channels).
+template <int HD, int GM>
+struct WarpState {
+    static constexpr int CPL = HDT<HD>::CPL;
+    static constexpr int NP = CPL >= 2 ? CPL / 2 : 1;
+    float m[GM], l[GM], sws[GM], spz[GM];
+    u64 acc2[GM][NP];   // CPL >= 2
+    float acc1[GM];     // CPL == 1
+    __device__ __forceinline__ void init() {
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            m[g] = -INFINITY; l[g] = 0.f; sws[g] = 0.f; spz[g] = 0.f; acc1[g] = 0.f;
+#pragma unroll
+            for (int p = 0; p < NP; ++p) acc2[g][p] = 0ull;
+        }
+    }
+};
+
+// online softmax update for one 32-token unit; returns p[g] for this lane's token
+template <int HD, int GM>
+__device__ __forceinline__ void softmax_update(WarpState<HD, GM>& S, const float (&s)[GM], float (&p)[GM]) {
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+        const float mu = warp_max_redux(s[g]);
+        const float mn = fmaxf(S.m[g], mu);
+        float alpha = 1.f, pv = 0.f;
+        if (mn != -INFINITY) {
+            alpha = exp2f(S.m[g] - mn);
+            pv = s[g] == -INFINITY ? 0.f : exp2f(s[g] - mn);
+        }
+        S.m[g] = mn;
+        S.l[g] = fmaf(S.l[g], alpha, pv);
+        S.sws[g] *= alpha;
+        S.spz[g] *= alpha;
+        if constexpr (WarpState<HD, GM>::CPL >= 2) {
+            const u64 a2 = f2pack(alpha, alpha);
+#pragma unroll
+            for (int q = 0; q < WarpState<HD, GM>::NP; ++q) S.acc2[g][q] = fmul2(S.acc2[g][q], a2);
+        } else {
+            S.acc1[g] *= alpha;
+        }
+        p[g] = pv;
+    }
+}
+
+// Sum of v[0..N) over the warp, scattered: lane l ends with the total of value
+// (l >> (5 - log2 N)) ... returned through `out` written to shared memory.
+template <int N>
+__device__ __forceinline__ void warp_reduce_scatter_to_smem(float (&v)[N], float* out, int lane) {
+    static_assert((N & (N - 1)) == 0 && N <= 32, "power of two");
+    int cnt = N;
+    int idx = 0;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (cnt > 1) {
+            const int half = cnt / 2;
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                if (i < half) {
+                    const float send = up ? v[i] : v[i + half];
+                    const float keep = up ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            if (up) idx += half;
+            cnt = half;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
+    // every lane holds the full total of value idx; the lowest such lane stores it
+    const int lanes_per_value = 32 / N;
+    if ((lane & (lanes_per_value - 1)) == 0) out[idx] = v[0];
+}
+
+// the GM (w, w) pairs of one token from the ws table, 16 bytes per load
+template <int GM>
+__device__ __forceinline__ void load_wrow(const u64* wt, u64 (&w)[GM]) {
+    if constexpr (GM % 2 == 0) {
+#pragma unroll
+        for (int g2 = 0; g2 < GM / 2; ++g2) {
+            const ulonglong2 x = reinterpret_cast<const ulonglong2*>(wt)[g2];
+            w[2 * g2] = x.x;
+            w[2 * g2 + 1] = x.y;
+        }
+    } else {
+        w[0] = wt[0];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// packed chunk
+// ---------------------------------------------------------------------------
+template <int HD, int GM>
+__device__ __forceinline__ void pbs_issue_stage(const JobDesc& J, int HG, int hg, int t0, int t1, int s,
+                                                unsigned char* stages, const StageLayout& SL, uint64_t* bars,
+                                                int lane) {
+    constexpr int DQ = HDT<HD>::DQ;
+    const int ST = stage_tokens(HG);
+    const int s0 = t0 + s * ST;
+    const int nt = min(ST, t1 - s0);
+    const int grp = J.grp, nkv = J.nkv, h0 = hg * HG;
+    // Every copy below starts 16-byte aligned and moves a multiple of 16 bytes:
+    // HG == nkv gives one contiguous run per region; otherwise HG == 8 and the
+    // per-row / per-block / per-token slices are HG*HD*4, HG*HD*mb, HG*HD/4 and
+    // HG*mb >= 16 bytes (plan_attention guarantees one of the two).
+    const int mb = J.meta16 ? 2 : 4;
+    const int rows = nt / 16, blks = nt / grp;
+    unsigned char* buf = stages + (size_t)(s % NSTAGE) * SL.bytes;
+    uint64_t* bar = &bars[s % NSTAGE];
+    const uint32_t bytes = (uint32_t)rows * HG * HD * 4 + 2u * blks * HG * HD * mb + (uint32_t)nt * HG * DQ * 4 +
+                           2u * nt * HG * mb + (uint32_t)nt * 8;
+    if (lane == 0) mbar_expect_tx(bar, bytes);
+    __syncwarp();
+    const char* kp = reinterpret_cast<const char*>(J.kp);
+    const char* ks = reinterpret_cast<const char*>(J.ks);
+    const char* kz = reinterpret_cast<const char*>(J.kz);
+    const char* vp = reinterpret_cast<const char*>(J.vp);
+    const char* vs = reinterpret_cast<const char*>(J.vs);
+    const char* vz = reinterpret_cast<const char*>(J.vz);
+    const char* ids = reinterpret_cast<const char*>(J.ids);
+    if (HG == nkv) {
+        if (lane == 0) tma_load_1d(buf + SL.kw, kp + (size_t)(s0 / 16) * nkv * HD * 4, rows * HG * HD * 4, bar);
+        if (lane == 1) tma_load_1d(buf + SL.ks, ks + (size_t)(s0 / grp) * nkv * HD * mb, blks * HG * HD * mb, bar);
+        if (lane == 2) tma_load_1d(buf + SL.kz, kz + (size_t)(s0 / grp) * nkv * HD * mb, blks * HG * HD * mb, bar);
+        if (lane == 3) tma_load_1d(buf + SL.vw, vp + (size_t)s0 * nkv * DQ * 4, nt * HG * DQ * 4, bar);
+        if (lane == 4) tma_load_1d(buf + SL.vs, vs + (size_t)s0 * nkv * mb, nt * HG * mb, bar);
+        if (lane == 5) tma_load_1d(buf + SL.vz, vz + (size_t)s0 * nkv * mb, nt * HG * mb, bar);
+        if (lane == 6) tma_load_1d(buf + SL.ids, ids + (size_t)s0 * 8, nt * 8, bar);
+    } else {
+        for (int i = lane; i < rows; i += 32)
+            tma_load_1d(buf + SL.kw + (size_t)i * HG * HD * 4, kp + ((size_t)(s0 / 16 + i) * nkv + h0) * HD * 4,
+                        HG * HD * 4, bar);
+        for (int i = lane; i < blks; i += 32) {
+            const size_t off = ((size_t)(s0 / grp + i) * nkv + h0) * HD * mb;
+            tma_load_1d(buf + SL.ks + (size_t)i * HG * HD * mb, ks + off, HG * HD * mb, bar);
+            tma_load_1d(buf + SL.kz + (size_t)i * HG * HD * mb, kz + off, HG * HD * mb, bar);
+        }
+        for (int i = lane; i < nt; i += 32) {
+            tma_load_1d(buf + SL.vw + (size_t)i * HG * DQ * 4, vp + ((size_t)(s0 + i) * nkv + h0) * DQ * 4,
+                        HG * DQ * 4, bar);
+            const size_t mo = ((size_t)(s0 + i) * nkv + h0) * mb;
+            tma_load_1d(buf + SL.vs + (size_t)i * HG * mb, vs + mo, HG * mb, bar);
+            tma_load_1d(buf + SL.vz + (size_t)i * HG * mb, vz + mo, HG * mb, bar);
+        }
+        if (lane == 0) tma_load_1d(buf + SL.ids, ids + (size_t)s0 * 8, nt * 8, bar);
+    }
+}
+
+template <int HD, int GM>
+__device__ __forceinline__ void pbs_unit(const JobDesc& J, int HG, int G, int kvl, int kvh, int lane, int D,
+                                         const unsigned char* buf, const StageLayout& SL, int s0, int nt, int r,
+                                         const float* qk, unsigned char* wa, float sc, WarpState<HD, GM>& S) {
+    constexpr int CPL = HDT<HD>::CPL, DQ = HDT<HD>::DQ;
+    using WA = WarpArea<HD, GM>;
+    float* qs_tab = reinterpret_cast<float*>(wa);
+    u64* ws_tab = reinterpret_cast<u64*>(wa + WA::qs);
+    float* bias = reinterpret_cast<float*>(wa + WA::qs + WA::ws);
+    const int grp = J.grp;
+    const int mb = J.meta16 ? 2 : 4;
+    const int ub = r * 32;  // unit start within the stage
+    const uint32_t* kw_s = reinterpret_cast<const uint32_t*>(buf + SL.kw);
+    const unsigned char* ks_s = buf + SL.ks;
+    const unsigned char* kz_s = buf + SL.kz;
+    const uint32_t* vw_s = reinterpret_cast<const uint32_t*>(buf + SL.vw);
+    const unsigned char* vs_s = buf + SL.vs;
+    const unsigned char* vz_s = buf + SL.vz;
+    const int64_t* ids_s = reinterpret_cast<const int64_t*>(buf + SL.ids);
+
+    // ---- qs = q*scale tables and per-block bias sums ----
+    // lane <-> channels lane, lane+32, ...: consecutive lanes touch consecutive
+    // shared-memory words (metadata, q) and write whole GM-wide table rows.
+    float part[4 * GM];  // [half][qs-sum | qz-sum][g]
+#pragma unroll
+    for (int i = 0; i < 4 * GM; ++i) part[i] = 0.f;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int tb = ub + hf * 16;
+        if (tb < nt) {
+            const int mblk = tb / grp;
+            const size_t mo = ((size_t)mblk * HG + kvl) * HD;
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+                const int c = lane + 32 * j;
+                if (c < HD) {
+                    const float sv = load_meta(ks_s, mo + c, mb == 2);
+                    const float zv = load_meta(kz_s, mo + c, mb == 2);
+                    float v[GM];
+#pragma unroll
+                    for (int g = 0; g < GM; ++g) {
+                        const float qv = qk[g * HD + c];
+                        v[g] = qv * sv;
+                        part[(hf * 2 + 0) * GM + g] += v[g];
+                        part[(hf * 2 + 1) * GM + g] = fmaf(qv, zv, part[(hf * 2 + 1) * GM + g]);
+                    }
+                    float* dst = qs_tab + (size_t)(hf * HD + c) * GM;
+                    if constexpr (GM % 4 == 0) {
+#pragma unroll
+                        for (int g4 = 0; g4 < GM / 4; ++g4)
+                            reinterpret_cast<float4*>(dst)[g4] =
+                                make_float4(v[4 * g4], v[4 * g4 + 1], v[4 * g4 + 2], v[4 * g4 + 3]);
+                    } else if constexpr (GM == 2) {
+                        *reinterpret_cast<float2*>(dst) = make_float2(v[0], v[1]);
+                    } else {
+                        dst[0] = v[0];
+                    }
+                }
+            }
+        }
+    }
+    warp_reduce_scatter_to_smem<4 * GM>(part, bias, lane);
+    __syncwarp();
+
+    // ---- QK: lane <-> token ----
+    const int tl = ub + lane;  // token within the stage
+    const bool inr = tl < nt;
+    const int hf = lane >> 4;
+    const int rot = (21 - 2 * (lane & 15)) & 31;
+    float s[GM];
+    {
+        const int row = inr ? (tl >> 4) : (ub >> 4);
+        const uint4* kw4 = reinterpret_cast<const uint4*>(kw_s + ((size_t)row * HG + kvl) * HD);
+        const float* qsh = qs_tab + (size_t)hf * HD * GM;
+        // two accumulator sets (even / odd channel quads) for independent FMA chains
+        constexpr int NG2 = GM >= 2 ? GM / 2 : 1;
+        u64 a2[2][NG2];
+        float a1[2] = {0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+#pragma unroll
+            for (int g2 = 0; g2 < NG2; ++g2) a2[e][g2] = 0ull;
+#pragma unroll 2
+        for (int c4 = 0; c4 < HD / 4; ++c4) {
+            const uint4 w4 = kw4[c4];
+            const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+            const int e = c4 & 1;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const float F = unpack_4pc(ww[jj], rot);
+                const float* qc = qsh + (c4 * 4 + jj) * GM;
+                if constexpr (GM == 1) {
+                    a1[e] = fmaf(qc[0], F, a1[e]);
+                } else {
+                    const u64 FF = f2pack(F, F);
+                    if constexpr (GM % 4 == 0) {
+#pragma unroll
+                        for (int g4 = 0; g4 < GM / 4; ++g4) {
+                            const ulonglong2 q4 = reinterpret_cast<const ulonglong2*>(qc)[g4];
+                            a2[e][2 * g4] = ffma2(q4.x, FF, a2[e][2 * g4]);
+                            a2[e][2 * g4 + 1] = ffma2(q4.y, FF, a2[e][2 * g4 + 1]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int g2 = 0; g2 < NG2; ++g2)
+                            a2[e][g2] = ffma2(*reinterpret_cast<const u64*>(qc + 2 * g2), FF, a2[e][g2]);
+                    }
+                }
+            }
+        }
+        const bool live = inr && ids_s[tl] != -1;
+        const float* bsh = bias + hf * 2 * GM;
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            float a;
+            if constexpr (GM == 1) {
+                a = a1[0] + a1[1];
+            } else {
+                const float2 v0 = f2unpack(a2[0][g / 2]), v1 = f2unpack(a2[1][g / 2]);
+                a = (g & 1) ? (v0.y + v1.y) : (v0.x + v1.x);
+            }
+            s[g] = live ? ((a - 4.0f * bsh[g]) + bsh[GM + g]) * sc : -INFINITY;
+        }
+    }
+    // ---- logits to scratch ----
+    if (inr) {
+        const int pos = D + s0 + tl;
+#pragma unroll
+        for (int g = 0; g < GM; ++g)
+            if (g < G) J.scores[(size_t)(kvh * G + g) * J.score_stride + pos] = s[g];
+    }
+    // ---- softmax, V weights ----
+    float p[GM];
+    softmax_update<HD, GM>(S, s, p);
+    float vsc = 0.f, vzr = 0.f;
+    if (inr) {
+        vsc = load_meta(vs_s, (size_t)tl * HG + kvl, mb == 2);
+        vzr = load_meta(vz_s, (size_t)tl * HG + kvl, mb == 2);
+    }
+    {
+        u64 wrow[GM];
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            const float w = p[g] * vsc;
+            S.sws[g] += w;
+            S.spz[g] = fmaf(p[g], vzr, S.spz[g]);
+            wrow[g] = f2pack(w, w);
+        }
+        u64* dst = ws_tab + lane * GM;
+        if constexpr (GM % 2 == 0) {
+#pragma unroll
+            for (int g2 = 0; g2 < GM / 2; ++g2) reinterpret_cast<ulonglong2*>(dst)[g2] = make_ulonglong2(wrow[2 * g2], wrow[2 * g2 + 1]);
+        } else {
+            dst[0] = wrow[0];
+        }
+    }
+    __syncwarp();
+    // ---- PV: lane <-> channels ----
+    const int ntu = min(32, nt - ub);
+    const int c0 = min(lane * CPL, HD - 1);
+    const int wi = c0 / 16;
+    int rotc[CPL];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) rotc[j] = (21 - 2 * ((c0 + j) & 15)) & 31;
+#pragma unroll 2
+    for (int t = 0; t < ntu; ++t) {
+        const uint32_t w = vw_s[((size_t)(ub + t) * HG + kvl) * DQ + wi];
+        const u64* wt = ws_tab + t * GM;
+        u64 wrow[GM];
+        load_wrow<GM>(wt, wrow);
+        if constexpr (CPL >= 2) {
+            u64 F2[CPL / 2];
+#pragma unroll
+            for (int q = 0; q < CPL / 2; ++q) F2[q] = f2pack(unpack_4pc(w, rotc[2 * q]), unpack_4pc(w, rotc[2 * q + 1]));
+#pragma unroll
+            for (int g = 0; g < GM; ++g) {
+                const u64 wg = wrow[g];
+#pragma unroll
+                for (int q = 0; q < CPL / 2; ++q) S.acc2[g][q] = ffma2(wg, F2[q], S.acc2[g][q]);
+            }
+        } else {
+            const float F = unpack_4pc(w, rotc[0]);
+#pragma unroll
+            for (int g = 0; g < GM; ++g) S.acc1[g] = fmaf(f2unpack(wt[g]).x, F, S.acc1[g]);
+        }
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// dense chunk: 32-token units, QK with lane <-> (token of 8, channel quarter)
+// ---------------------------------------------------------------------------
+template <int HD, int GM>
+__device__ __forceinline__ void dense_unit(const JobDesc& J, const TierCounts& tc, int G, int kvh, int lane, int ub,
+                                           int t1, const float* qk, unsigned char* wa, float sc,
+                                           WarpState<HD, GM>& S) {
+    constexpr int CPL = HDT<HD>::CPL;
+    using WA = WarpArea<HD, GM>;
+    u64* ws_tab = reinterpret_cast<u64*>(wa + WA::qs);
+    float* sc_tab = reinterpret_cast<float*>(wa + WA::sc);
+    const float** vrow = reinterpret_cast<const float**>(wa + WA::vrow);
+    const size_t kvs = (size_t)J.nkv * HD;
+    const int jt = lane >> 2, qq = lane & 3;
+    constexpr int CH = HD >= 16 ? HD / 16 : 1;  // float4 chunks per quarter
+#pragma unroll 1
+    for (int rd = 0; rd < 4; ++rd) {
+        const int tk = ub + rd * 8 + jt;
+        float a[GM];
+#pragma unroll
+        for (int g = 0; g < GM; ++g) a[g] = 0.f;
+        if (tk < t1) {
+            const float *Kb, *Vb;
+            int slot;
+            dense_slot(J, tc, tk, Kb, Vb, slot);
+            const float* krow = Kb + (size_t)slot * kvs + (size_t)kvh * HD;
+            if (qq == 0) vrow[rd * 8 + jt] = Vb + (size_t)slot * kvs + (size_t)kvh * HD;
+            float4 k4[CH];
+#pragma unroll
+            for (int i = 0; i < CH; ++i) k4[i] = __ldg(reinterpret_cast<const float4*>(krow) + 4 * i + qq);
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+#pragma unroll
+                for (int g = 0; g < GM; ++g) {
+                    const float4 q = reinterpret_cast<const float4*>(qk + g * HD)[4 * i + qq];
+                    a[g] = fmaf(q.x, k4[i].x, a[g]);
+                    a[g] = fmaf(q.y, k4[i].y, a[g]);
+                    a[g] = fmaf(q.z, k4[i].z, a[g]);
+                    a[g] = fmaf(q.w, k4[i].w, a[g]);
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            a[g] += __shfl_xor_sync(0xffffffffu, a[g], 1);
+            a[g] += __shfl_xor_sync(0xffffffffu, a[g], 2);
+        }
+        if (qq == 0) {
+#pragma unroll
+            for (int g = 0; g < GM; ++g) sc_tab[(rd * 8 + jt) * GM + g] = a[g];
+        }
+    }
+    __syncwarp();
+    const int tk = ub + lane;
+    const bool inr = tk < t1;
+    float s[GM];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) s[g] = inr ? sc_tab[lane * GM + g] * sc : -INFINITY;
+    if (inr) {
+#pragma unroll
+        for (int g = 0; g < GM; ++g)
+            if (g < G) J.scores[(size_t)(kvh * G + g) * J.score_stride + tk] = s[g];
+    }
+    float p[GM];
+    softmax_update<HD, GM>(S, s, p);
+#pragma unroll
+    for (int g = 0; g < GM; ++g) ws_tab[lane * GM + g] = f2pack(p[g], p[g]);
+    __syncwarp();
+    const int ntu = min(32, t1 - ub);
+    const int c0 = lane * CPL;
+#pragma unroll 4
+    for (int t = 0; t < ntu; ++t) {
+        const float* vr = vrow[t] + c0;
+        const u64* wt = ws_tab + t * GM;
+        u64 wrow[GM];
+        load_wrow<GM>(wt, wrow);
+        if constexpr (CPL >= 2) {
+            u64 v2[CPL / 2];
+            if constexpr (CPL % 4 == 0) {
+#pragma unroll
+                for (int q = 0; q < CPL / 4; ++q) {
+                    const float4 x = ldg_stream_f4(vr + 4 * q);
+                    v2[2 * q] = f2pack(x.x, x.y);
+                    v2[2 * q + 1] = f2pack(x.z, x.w);
+                }
+            } else {
+                const float2 x = __ldg(reinterpret_cast<const float2*>(vr));
+                v2[0] = f2pack(x.x, x.y);
+            }
+#pragma unroll
+            for (int g = 0; g < GM; ++g) {
+                const u64 wg = wrow[g];
+#pragma unroll
+                for (int q = 0; q < CPL / 2; ++q) S.acc2[g][q] = ffma2(wg, v2[q], S.acc2[g][q]);
+            }
+        } else {
+            const float v = c0 < HD ? __ldg(vr) : 0.f;
+#pragma unroll
+            for (int g = 0; g < GM; ++g) S.acc1[g] = fmaf(f2unpack(wt[g]).x, v, S.acc1[g]);
+        }
+    }
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int HD, int GM>
+__global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __grid_constant__ AttnLaunch L) {
+    constexpr int CPL = HDT<HD>::CPL;
+    using WA = WarpArea<HD, GM>;
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ JobDesc Js;
+    __shared__ TierCounts Ts;
+    __shared__ __align__(8) uint64_t bars[NSTAGE];
+
+    const int job = blockIdx.y / L.nhg;
+    const int hg = blockIdx.y - job * L.nhg;
+    if (threadIdx.x == 0) {
+        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
+        Ts = resolve_counts(Js);
+    }
+    __syncthreads();
+    const JobDesc& J = Js;
+    const TierCounts tc = Ts;
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const int ntok = tc.nblk * J.grp;
+    const bool is_dense = (int)blockIdx.x < L.nd;
+    int t0, t1;
+    if (is_dense) {
+        t0 = blockIdx.x * L.DC;
+        t1 = min(D, t0 + L.DC);
+    } else {
+        t0 = (blockIdx.x - L.nd) * L.PC;
+        t1 = min(ntok, t0 + L.PC);
+    }
+    if (t0 >= t1) return;
+
+    const int nq = J.nq, G = L.G, HG = L.HG;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kvl = warp % HG, r0 = warp / HG, WPH = NW / HG;
+    const bool active = warp < HG * WPH;  // with 3, 5, 6 or 7 heads some warps idle
+    const int kvh = hg * HG + kvl;
+    const float sc = (1.0f / sqrtf((float)HD)) * kLog2e;  // log2-domain logit scale
+    const int mb = J.meta16 ? 2 : 4;
+    const StageLayout SL = stage_layout(HD, mb);
+    const int qbytes = align_up(HG * GM * HD * 4, 128);
+    unsigned char* stages = smem + qbytes;
+    unsigned char* wa = stages + (size_t)NSTAGE * SL.bytes + (size_t)warp * WA::bytes;
+
+    // packed chunks: start the first copies before staging Q
+    const int ST = stage_tokens(HG);
+    const int nst = is_dense ? 0 : ceil_div(t1 - t0, ST);
+    if (!is_dense) {
+        if (threadIdx.x == 0) {
+#pragma unroll
+            for (int i = 0; i < NSTAGE; ++i) mbar_init(&bars[i], 1);
+            mbar_fence_init();
+        }
+        __syncthreads();
+        if (warp == 0)
+            for (int s = 0; s < NSTAGE && s < nst; ++s)
+                pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s, stages, SL, bars, lane);
+    }
+
+    // ---- query rows of this kv-head group: q_s[kvl][g][c] ----
+    float* q_s = reinterpret_cast<float*>(smem);
+    const float* __restrict__ Q = L.Q[job];
+    for (int i = threadIdx.x; i < HG * GM * HD; i += NT) {
+        const int c = i % HD, kg = i / HD, g = kg % GM, kv = kg / GM;
+        q_s[i] = g < G ? Q[((size_t)(hg * HG + kv) * G + g) * HD + c] : 0.f;
+    }
+    __syncthreads();
+    const float* qk = q_s + (size_t)kvl * GM * HD;
+
+    WarpState<HD, GM> S;
+    S.init();
+    bool failed = false;
+    if (is_dense) {
+        if (active)
+            for (int u = r0; t0 + u * 32 < t1; u += WPH)
+                dense_unit<HD, GM>(J, tc, G, kvh, lane, t0 + u * 32, t1, qk, wa, sc, S);
+    } else {
+        int s = 0;
+        for (; s < nst; ++s) {
+            const bool ok = mbar_wait_bounded(&bars[s % NSTAGE], (uint32_t)((s / NSTAGE) & 1));
+            if (__syncthreads_or(!ok)) {
+                failed = true;
+                break;
+            }
+            const unsigned char* buf = stages + (size_t)(s % NSTAGE) * SL.bytes;
+            const int s0 = t0 + s * ST;
+            const int nt = min(ST, t1 - s0);
+            if (active && r0 * 32 < nt) pbs_unit<HD, GM>(J, HG, G, kvl, kvh, lane, D, buf, SL, s0, nt, r0, qk, wa, sc, S);
+            __syncthreads();
+            if (warp == 0 && s + NSTAGE < nst) pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s + NSTAGE, stages, SL, bars, lane);
+        }
+        if (failed) {
+            // drain this CTA's own copies in flight, then give up on the chunk
+            for (int k = s; k < nst && k < s + NSTAGE; ++k)
+                (void)mbar_wait_bounded(&bars[k % NSTAGE], (uint32_t)((k / NSTAGE) & 1));
+            if (threadIdx.x == 0) {
+                atomicCAS(&g_device_error, 0, (int)TT_ERR_TIMEOUT);
+                if (J.ctr) atomicCAS(const_cast<int*>(&J.ctr->error), 0, (int)TT_ERR_TIMEOUT);
+            }
+            return;
+        }
+    }
+
+    // ---- per-warp totals ----
+    float out[GM][CPL];
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+        S.l[g] = warp_sum(S.l[g]);
+        float SW = 0.f, SZ = 0.f;
+        if (!is_dense) {
+            SW = warp_sum(S.sws[g]);
+            SZ = warp_sum(S.spz[g]);
+        }
+        if constexpr (CPL >= 2) {
+#pragma unroll
+            for (int q = 0; q < CPL / 2; ++q) {
+                const float2 v = f2unpack(S.acc2[g][q]);
+                out[g][2 * q] = v.x;
+                out[g][2 * q + 1] = v.y;
+            }
+        } else {
+            out[g][0] = S.acc1[g];
+        }
+        if (!is_dense) {
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) out[g][j] = (out[g][j] - 4.0f * SW) + SZ;
+        }
+    }
+
+    const int chunk = blockIdx.x;
+    if (WPH == 1) {
+        if (!active) return;
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            if (g >= G) break;
+            const size_t pi = (size_t)chunk * nq + (size_t)kvh * G + g;
+            if (lane == 0) {
+                J.part_ml[pi * 2 + 0] = S.m[g];
+                J.part_ml[pi * 2 + 1] = S.l[g];
+            }
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+                const int c = lane * CPL + j;
+                if (c < HD) J.part_acc[pi * HD + c] = out[g][j];
+            }
+        }
+        return;
+    }
+    // ---- merge the WPH warps that share a kv head (buffer aliases the stages) ----
+    __syncthreads();
+    float* mbuf = reinterpret_cast<float*>(smem + qbytes);
+    float* mine = mbuf + (size_t)warp * GM * (HD + 2);
+#pragma unroll
+    for (int g = 0; g < GM; ++g) {
+        if (lane == 0) {
+            mine[g * (HD + 2) + 0] = S.m[g];
+            mine[g * (HD + 2) + 1] = S.l[g];
+        }
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+            const int c = lane * CPL + j;
+            if (c < HD) mine[g * (HD + 2) + 2 + c] = out[g][j];
+        }
+    }
+    __syncthreads();
+    if (r0 != 0 || !active) return;
+    for (int g = 0; g < G && g < GM; ++g) {
+        float M = -INFINITY;
+        for (int r = 0; r < WPH; ++r) M = fmaxf(M, mbuf[(size_t)(r * HG + kvl) * GM * (HD + 2) + g * (HD + 2)]);
+        float Ls = 0.f;
+        float o[CPL];
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) o[j] = 0.f;
+        for (int r = 0; r < WPH; ++r) {
+            const float* src = mbuf + (size_t)(r * HG + kvl) * GM * (HD + 2) + g * (HD + 2);
+            const float mr = src[0];
+            if (mr == -INFINITY) continue;
+            const float f = exp2f(mr - M);
+            Ls = fmaf(src[1], f, Ls);
+#pragma unroll
+            for (int j = 0; j < CPL; ++j) {
+                const int c = lane * CPL + j;
+                if (c < HD) o[j] = fmaf(src[2 + c], f, o[j]);
+            }
+        }
+        const size_t pi = (size_t)chunk * nq + (size_t)kvh * G + g;
+        if (lane == 0) {
+            J.part_ml[pi * 2 + 0] = M;
+            J.part_ml[pi * 2 + 1] = Ls;
+        }
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+            const int c = lane * CPL + j;
+            if (c < HD) J.part_acc[pi * HD + c] = o[j];
+        }
+    }
+}
+
+}  // namespace tt
