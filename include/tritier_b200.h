@@ -96,6 +96,30 @@ tt_status tt_fused_attention_decode(
     int head_dim, float* attn_output, float* mean_attn_weights, int k_group_size,
     int meta_fp16, void* stream);
 
+/* Same arguments, layouts and results as tt_fused_attention_decode, but the
+ * call allocates nothing: its scratch is a fixed 32 MiB array in device
+ * memory, declared at file scope in the library, instead of a workspace grown
+ * with cudaMalloc.  It is for callers that must not allocate device memory
+ * after start-up (a process that reserves the GPU's memory up front, a host
+ * framework whose allocator owns device memory, a loop where cudaMalloc's
+ * possible device synchronisation is not acceptable).  Calls whose scratch
+ * need (partials of every split-KV chunk plus num_q_heads x tokens logits)
+ * exceeds 32 MiB return TT_ERR_INVALID_ARGUMENT with a message.  Every call
+ * on a device shares the one array and leaves its contents behind, so calls
+ * that overlap on the GPU (different streams, or threads) race; keep them
+ * ordered.  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every GPU that loads the library holds the array until the process exits.
+ * No counterpart in the reference (its CPU kernel keeps thread-local scratch
+ * vectors, fused_attn_avx2.cpp:139-143). */
+tt_status tt_fused_attention_decode_noalloc(
+    const float* Q, const float* dense_K, const float* dense_V, int dense_count,
+    const int32_t* PBS_K_Packed, const void* PBS_K_Scales, const void* PBS_K_Zeroes,
+    const int32_t* PBS_V_Packed, const void* PBS_V_Scales, const void* PBS_V_Zeroes,
+    const int64_t* PBS_token_ids, int num_blocks, int num_q_heads, int num_kv_heads,
+    int head_dim, float* attn_output, float* mean_attn_weights, int k_group_size,
+    int meta_fp16, void* stream);
+
 /* One K block: K [k_group_size, num_heads, head_dim] -> packed
  * [k_group_size/16, num_heads, head_dim] words, scale/zero [num_heads, head_dim].
  * Bit-exact with quantize_k_block_avx2 (csrc/include/quantize_k_avx2.h:4-20;

@@ -61,7 +61,7 @@ EXPORTS = [
     "tt_engine_destroy", "tt_engine_step", "tt_engine_step_batched", "tt_engine_prefill",
     "tt_engine_get_counters", "tt_engine_get_buffer", "tt_engine_get_buffer_bytes",
     "tt_engine_device_bytes", "tt_engine_set_counters", "tt_profile_enable", "tt_profile_collect",
-    "tt_device_error",
+    "tt_device_error", "tt_fused_attention_decode_noalloc",
 ]
 
 _lib = None
@@ -95,6 +95,8 @@ def _declare(L):
     L.tt_profile_enable.argtypes = [i]
     L.tt_profile_collect.argtypes = [C.POINTER(KernelTimes)]
     L.tt_device_error.argtypes = [i, C.POINTER(i)]
+    L.tt_fused_attention_decode_noalloc.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, vp, i,
+                                                    i, vp]
     for name in EXPORTS:
         if name not in ("tt_last_error", "tt_version"):
             getattr(L, name).restype = C.c_int
