@@ -15,7 +15,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 SOURCES = ["tt_api.cu", "tt_attn.cu", "tt_engine.cu", "tt_noalloc.cu"]
-HEADERS = ["tt_common.cuh", "tt_attn.cuh", os.path.join("..", "..", "include", "tritier_b200.h")]
+HEADERS = ["tt_common.cuh", "tt_attn.cuh", "tt_partial.cuh", "tt_pbs_mma.cuh",
+           os.path.join("..", "..", "include", "tritier_b200.h")]
 LIB = os.path.join(PKG, "libtritier_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

@@ -201,35 +201,46 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
     return TT_OK;
 }
 
-template <int HD, int GM>
+template <int HD, int GM, bool MMA>
 static tt_status launch_partial_t(const AttnLaunch& L, cudaStream_t st) {
-    const size_t sm = partial_smem_bytes<HD, GM>(L.HG, L.meta_bytes);
+    const size_t sm = partial_smem_bytes<HD, GM, MMA>(L.HG, L.meta_bytes);
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
         size_t mx = 0;
-        for (int hg = 1; hg <= 8; hg *= 2) mx = std::max(mx, partial_smem_bytes<HD, GM>(hg, 4));
-        cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD, GM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        for (int hg = 1; hg <= 8; hg *= 2) mx = std::max(mx, partial_smem_bytes<HD, GM, MMA>(hg, 4));
+        cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD, GM, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)mx);
         if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(k_attn_partial)");
         configured[dev & 63] = true;
     }
     dim3 grid(L.nd + L.np, L.njobs * L.nhg);
     const int ps = prof_begin(1, st);
-    k_attn_partial<HD, GM><<<grid, NT, sm, st>>>(L);
+    k_attn_partial<HD, GM, MMA><<<grid, NT, sm, st>>>(L);
     prof_end(ps, st);
     return check_launch("k_attn_partial");
+}
+
+// Packed chunks run on the tensor cores (mma.sync f16) for head_dim 64 / 128,
+// up to 4 query heads per kv head and fp16 metadata in every job of the
+// batch; other shapes keep the SIMT unit.
+template <int HD, int GM>
+static tt_status launch_partial_g(const AttnLaunch& L, cudaStream_t st) {
+    if constexpr ((HD == 64 || HD == 128) && GM <= 4) {
+        if (L.meta_bytes == 2) return launch_partial_t<HD, GM, true>(L, st);
+    }
+    return launch_partial_t<HD, GM, false>(L, st);
 }
 
 template <int HD>
 static tt_status launch_partial_hd(const AttnLaunch& L, cudaStream_t st) {
     switch (pick_gm(L.G)) {
-        case 1: return launch_partial_t<HD, 1>(L, st);
-        case 2: return launch_partial_t<HD, 2>(L, st);
-        case 4: return launch_partial_t<HD, 4>(L, st);
+        case 1: return launch_partial_g<HD, 1>(L, st);
+        case 2: return launch_partial_g<HD, 2>(L, st);
+        case 4: return launch_partial_g<HD, 4>(L, st);
         case 8:
-            if constexpr (HD <= 128) return launch_partial_t<HD, 8>(L, st);
+            if constexpr (HD <= 128) return launch_partial_g<HD, 8>(L, st);
             return set_error(TT_ERR_UNSUPPORTED, "head_dim 256 supports at most 4 query heads per kv head");
     }
     return set_error(TT_ERR_UNSUPPORTED, "unsupported GQA ratio");

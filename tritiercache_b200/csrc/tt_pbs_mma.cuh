@@ -1,0 +1,362 @@
+// tt_pbs_mma.cuh -- packed-tier (2-bit) attention on the tensor cores with
+// mma.sync.m16n8k16 (f16 operands, f32 accumulation).  Included by
+// tt_partial.cuh.  Used for head_dim 64 / 128, at most 4 query heads per kv
+// head and fp16 metadata; the SIMT unit covers the other shapes.
+//
+// Fragment layout of m16n8k16 (row.col); lane = 4*gid + tig:
+//   A a0:(row gid, k-slots 2tig,2tig+1) a1:(gid+8, same) a2:(gid, 2tig+8,+9) a3:(gid+8, same)
+//   B b0:(k-slots 2tig,2tig+1; n=gid)   b1:(k-slots 2tig+8,+9; n=gid)
+//   D d0,d1:(row gid, n=2tig,2tig+1)    d2,d3:(row gid+8, same)
+// Any k-slot <-> element permutation works as long as A and B use the same
+// one: k-slots (2tig, 2tig+1, 2tig+8, 2tig+9) map to channels 16ks+4tig+{0..3}
+// in QK (one 16-byte load of K words, one 8-byte load of scales) and to tokens
+// tig+4i (i = 0..3) of a 16-token step in PV (bank-conflict-free V loads).
+//
+// Columns n = 2g + part: head g, part 0 = f16 "hi", part 1 = f16 "lo" of the
+// same f32 operand, so one f32 accumulation carries ~22 significant bits.
+//
+// QK per 16-token half-unit, score[t][g] = sum_c (q_c s_c) (4 + code_tc):
+//   A = 4 + code as f16 (exact): the 2-bit fields of rows gid and gid+8 sit in
+//       bytes gid/4 and 2+gid/4 of each K word (16 tokens of one channel);
+//       one PRMT gathers them from two words, a shift + LOP3 each places them
+//       in the mantissa of f16 4.0.
+//   B = q' * s split into hi/lo with f16 FMAs: h = q'h*s, r = q'h*s - h (exact),
+//       lo = q'l*s + r; q' = q * 2^-e_g with |q'| < 1, so |q' s| <= 65504.
+//   bias = -4 sum_c q' s + sum_c q' z: one MMA per k-step with the scale and
+//       zero rows of both blocks as A rows 0..3 and the q' fragments as B.
+// PV per 32-token unit, out[c][g] = sum_t (p_t vs_t) (4 + code_tc):
+//   A = 4 + code from the V words (16 channels of one token), same gather;
+//   B = p*vs*2^-E split hi/lo; E is kept while a unit's largest weight stays
+//   in [2^4, 2^14) * 2^E (else reset to put it near 2^13).  Each unit's
+//   tile result (hi + lo columns) is folded into the running f32 output as
+//   acc = acc * alpha * 2^(E_old - E_new) + tile.
+// In both D layouts a thread holds query head g = tig.
+#pragma once
+
+namespace tt {
+
+constexpr int kMmaWRow = 48;  // halves per row of the PV weight table (32 tokens + pad)
+
+template <int HD>
+struct MmaWarpArea {
+    static constexpr int wtab = 8 * kMmaWRow * 2;  // [n][position] f16
+    static constexpr int qtab = (HD / 16) * 32 * 4; // [ks][head*4 + tig][2] f16x2: q' hi
+    static constexpr int bytes = wtab + qtab;
+};
+
+// V words of one staged token occupy HG*DQ + 4 words (the pad spreads the four
+// tokens a load instruction touches over distinct banks).
+__host__ __device__ __forceinline__ int mma_vrow_words(int HG, int HD) { return HG * (HD / 16) + 4; }
+
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D = A*B (zero accumulator)
+__device__ __forceinline__ void mma_f16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }  // |e| <= 126
+
+// Two A registers (rows gid, gid+8) for the k-slot pair whose words are w0, w1:
+// sel gathers byte gid/4 and 2+gid/4 of both words, sft = 2*(gid%4).
+__device__ __forceinline__ void a_pair(uint32_t w0, uint32_t w1, uint32_t sel, int sft, uint32_t& lo_row,
+                                       uint32_t& hi_row) {
+    const uint32_t P = __byte_perm(w0, w1, sel);
+    lo_row = ((P << (8 - sft)) & 0x03000300u) | 0x44004400u;
+    hi_row = ((P >> sft) & 0x03000300u) | 0x44004400u;
+}
+
+// B register (n = gid) of q'*s for two channels: hi lanes h, lo lanes q'l*s + (q'h*s - h).
+__device__ __forceinline__ uint32_t b_qs(uint32_t qh, uint32_t qx, uint32_t s, uint32_t lomask) {
+    const __half2 sv = u2h(s), qhv = u2h(qh);
+    const __half2 h = __hmul2(qhv, sv);
+    const uint32_t r = h2u(__hfma2(qhv, sv, __hneg2(h))) & lomask;
+    return h2u(__hfma2(u2h(qx), sv, u2h(r)));
+}
+
+// Per-thread q' fragments for n = gid (head gid/2, part gid&1) and the
+// power-of-two scale of head tig.  The hi part, which both lanes of a head
+// need, sits in the warp's q table (qtab of MmaWarpArea).
+template <int HD>
+struct MmaQ {
+    static constexpr int KS = HD / 16;
+    uint32_t qx[KS][2];  // the B fragment of q' itself: hi (even gid) or lo (odd gid)
+    uint32_t lomask;     // all ones on odd gid
+    float up_sc;         // 2^e of head tig times the log2-domain logit scale
+};
+
+template <int HD, int GM>
+__device__ __forceinline__ void mma_prepare_q(const float* qk, int lane, float sc, unsigned char* wa, MmaQ<HD>& Q) {
+    constexpr int KS = HD / 16;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int g = gid >> 1;
+    float4 v[KS];
+    float mx = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+        v[ks] = g < GM ? *reinterpret_cast<const float4*>(qk + g * HD + 16 * ks + 4 * tig) : make_float4(0.f, 0.f, 0.f, 0.f);
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v[ks].x), fabsf(v[ks].y)), fmaxf(fabsf(v[ks].z), fabsf(v[ks].w))));
+    }
+    // lanes of one head differ in tig (xor 1, 2) and part (xor 4)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    // e with mx * 2^-e in [0.5, 1); zero rows keep e = 0
+    int e = mx > 0.f ? (int)((__float_as_uint(mx) >> 23) & 0xff) - 126 : 0;
+    e = max(-100, min(100, e));
+    const float down = pow2f(-e);
+    const bool odd = (gid & 1) != 0;
+    Q.lomask = odd ? 0xffffffffu : 0u;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+        const float x0 = v[ks].x * down, x1 = v[ks].y * down, x2 = v[ks].z * down, x3 = v[ks].w * down;
+        const __half2 h01 = __floats2half2_rn(x0, x1), h23 = __floats2half2_rn(x2, x3);
+        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+        const __half2 l01 = __floats2half2_rn(x0 - f01.x, x1 - f01.y), l23 = __floats2half2_rn(x2 - f23.x, x3 - f23.y);
+        if (!odd)
+            *reinterpret_cast<uint2*>(wa + MmaWarpArea<HD>::wtab + (size_t)(ks * 32 + (g * 4 + tig) * 2) * 4) =
+                make_uint2(h2u(h01), h2u(h23));
+        Q.qx[ks][0] = odd ? h2u(l01) : h2u(h01);
+        Q.qx[ks][1] = odd ? h2u(l23) : h2u(h23);
+    }
+    // head tig's exponent lives on lane 8*tig (gid = 2*tig)
+    const int et = __shfl_sync(0xffffffffu, e, 8 * tig);
+    Q.up_sc = pow2f(et) * sc;
+    __syncwarp();
+}
+
+template <int HD>
+struct MmaState {
+    static constexpr int MT = HD / 16;
+    float m, l, sws, spz;  // head tig; l / sws / spz over this thread's tokens only
+    int E;                 // exponent of the PV accumulator
+    float acc[MT][2];      // channels 16mt+gid and 16mt+gid+8 (hi + lo columns folded)
+    __device__ __forceinline__ void init() {
+        m = -INFINITY; l = 0.f; sws = 0.f; spz = 0.f; E = 0;
+#pragma unroll
+        for (int i = 0; i < MT; ++i) { acc[i][0] = 0.f; acc[i][1] = 0.f; }
+    }
+};
+
+// position of unit-local token t in the PV weight table (k-slot order)
+__device__ __forceinline__ int mma_wpos(int t) { return (t & 16) + 4 * (t & 3) + ((t & 15) >> 2); }
+
+__device__ __forceinline__ float ex2_approx(float x) {  // 2^x (PTX ex2.approx; -inf -> +0)
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+template <int HD, int GM>
+__device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, int kvl, int kvh, int lane, int D,
+                                             const unsigned char* buf, const StageLayout& SL, int s0, int nt, int r,
+                                             const MmaQ<HD>& Q, unsigned char* wa, MmaState<HD>& S) {
+    static_assert((HD == 64 || HD == 128) && GM <= 4, "tensor-core unit shape");
+    static_assert(MmaWarpArea<HD>::bytes <= WarpArea<HD, GM, true>::bytes, "weight table fits the warp area");
+    constexpr int KS = HD / 16, MT = HD / 16, DQ = HD / 16;
+    const int gid = lane >> 2, tig = lane & 3;
+    const int sft = 2 * (gid & 3);
+    const uint32_t sel = 0x6420u + 0x1111u * (uint32_t)(gid >> 2);
+    __half* wtab = reinterpret_cast<__half*>(wa);
+    const int gsh = J.grp == 32 ? 5 : 4;  // log2 of the block size (16 or 32)
+    const int ub = r * 32;  // unit start within the stage
+    const uint32_t* kw_s = reinterpret_cast<const uint32_t*>(buf + SL.kw);
+    const __half* ks_s = reinterpret_cast<const __half*>(buf + SL.ks);
+    const __half* kz_s = reinterpret_cast<const __half*>(buf + SL.kz);
+    const uint32_t* vw_s = reinterpret_cast<const uint32_t*>(buf + SL.vw);
+    const __half* vs_s = reinterpret_cast<const __half*>(buf + SL.vs);
+    const __half* vz_s = reinterpret_cast<const __half*>(buf + SL.vz);
+    const int64_t* ids_s = reinterpret_cast<const int64_t*>(buf + SL.ids);
+    // Second half-unit present?  (nt is a multiple of 16.)  When it is not,
+    // its rows still run through the MMAs on whatever the stage buffer holds
+    // (in bounds: ub + 32 <= ST); every value derived from them is masked.
+    const bool two = ub + 16 < nt;
+
+    // ---- bias rows and QK, three independent accumulation chains ----
+    // bias A rows 0..3: scale / zero of the block of half 0 / half 1
+    float bd[4] = {0.f, 0.f, 0.f, 0.f};
+    float dq[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+        const bool rowv = gid < 4;
+        const __half* mrow =
+            ((gid & 1) ? kz_s : ks_s) + ((size_t)((ub + 16 * ((gid >> 1) & 1)) >> gsh) * HG + kvl) * HD + 4 * tig;
+        const uint32_t* kw0 = kw_s + ((size_t)(ub >> 4) * HG + kvl) * HD + 4 * tig;
+        const uint32_t* kw1 = kw0 + (size_t)HG * HD;
+        const __half* sb0 = ks_s + ((size_t)(ub >> gsh) * HG + kvl) * HD + 4 * tig;
+        const __half* sb1 = ks_s + ((size_t)((ub + 16) >> gsh) * HG + kvl) * HD + 4 * tig;
+        const bool shared_blk = gsh == 5;  // both halves in one block: same B fragments
+        const uint32_t* qh_t = reinterpret_cast<const uint32_t*>(wa + MmaWarpArea<HD>::wtab) + ((gid >> 1) * 4 + tig) * 2;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            uint2 m2 = make_uint2(0u, 0u);
+            if (rowv) m2 = *reinterpret_cast<const uint2*>(mrow + 16 * ks);
+            mma_f16_16816(bd, m2.x, 0u, m2.y, 0u, Q.qx[ks][0], Q.qx[ks][1]);
+            const uint4 w0 = *reinterpret_cast<const uint4*>(kw0 + 16 * ks);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(kw1 + 16 * ks);
+            const uint2 sv0 = *reinterpret_cast<const uint2*>(sb0 + 16 * ks);
+            const uint2 qh = *reinterpret_cast<const uint2*>(qh_t + ks * 32);
+            const uint32_t b00 = b_qs(qh.x, Q.qx[ks][0], sv0.x, Q.lomask);
+            const uint32_t b01 = b_qs(qh.y, Q.qx[ks][1], sv0.y, Q.lomask);
+            uint32_t b10 = b00, b11 = b01;
+            if (!shared_blk) {
+                const uint2 sv1 = *reinterpret_cast<const uint2*>(sb1 + 16 * ks);
+                b10 = b_qs(qh.x, Q.qx[ks][0], sv1.x, Q.lomask);
+                b11 = b_qs(qh.y, Q.qx[ks][1], sv1.y, Q.lomask);
+            }
+            uint32_t a0, a1, a2, a3;
+            a_pair(w0.x, w0.y, sel, sft, a0, a1);
+            a_pair(w0.z, w0.w, sel, sft, a2, a3);
+            mma_f16_16816(dq[0], a0, a1, a2, a3, b00, b01);
+            a_pair(w1.x, w1.y, sel, sft, a0, a1);
+            a_pair(w1.z, w1.w, sel, sft, a2, a3);
+            mma_f16_16816(dq[1], a0, a1, a2, a3, b10, b11);
+        }
+    }
+    const float beta = bd[0] + bd[1];  // row gid, head tig
+    float s[4];  // unit-local tokens gid, gid+8, 16+gid, 24+gid; head tig
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const float bsum = __shfl_sync(0xffffffffu, beta, 8 * hf + tig);
+        const float bzer = __shfl_sync(0xffffffffu, beta, 8 * hf + 4 + tig);
+        const float bias = bzer - 4.0f * bsum;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int t = ub + 16 * hf + gid + 8 * j;  // stage-local token
+            const bool live = (hf == 0 || two) && tig < G && ids_s[t] != -1;
+            s[2 * hf + j] = live ? ((dq[hf][2 * j] + dq[hf][2 * j + 1]) + bias) * Q.up_sc : -INFINITY;
+        }
+    }
+    // ---- logits to scratch ----
+    if (tig < G) {
+        float* srow = J.scores + (size_t)(kvh * G + tig) * J.score_stride + D + s0 + ub;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int t = 16 * (k >> 1) + gid + 8 * (k & 1);
+            if (k < 2 || two) srow[t] = s[k];
+        }
+    }
+    // ---- online softmax for head tig ----
+    float mu = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
+    mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, 4));
+    mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, 8));
+    mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, 16));
+    const float mn = fmaxf(S.m, mu);
+    float alpha = 1.f;
+    float p[4] = {0.f, 0.f, 0.f, 0.f};
+    if (mn != -INFINITY) {
+        alpha = ex2_approx(S.m - mn);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) p[k] = ex2_approx(s[k] - mn);
+    }
+    S.m = mn;
+    S.l = fmaf(S.l, alpha, (p[0] + p[1]) + (p[2] + p[3]));
+    S.sws *= alpha;
+    S.spz *= alpha;
+    // ---- PV weights p*vs: running sums, accumulator exponent, hi/lo table ----
+    float ws[4];
+    float wmx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int t = ub + 16 * (k >> 1) + gid + 8 * (k & 1);
+        float vsc = 0.f, vzr = 0.f;
+        if (k < 2 || two) {
+            vsc = __half2float(vs_s[(size_t)t * HG + kvl]);
+            vzr = __half2float(vz_s[(size_t)t * HG + kvl]);
+        }
+        ws[k] = p[k] * vsc;
+        S.sws += ws[k];
+        S.spz = fmaf(p[k], vzr, S.spz);
+        wmx = fmaxf(wmx, fabsf(ws[k]));
+    }
+    // keep the exponent unless the unit's largest weight leaves [2^4, 2^14) * 2^E
+    const uint32_t wmb = __reduce_max_sync(0xffffffffu, __float_as_uint(wmx));
+    const int we = (int)((wmb >> 23) & 0xff) - 127;
+    int En = S.E;
+    if (wmb != 0u && (we - S.E >= 14 || we - S.E < 4)) En = max(-40, min(40, we - 13));
+    const float f = alpha * pow2f(S.E - En);
+    S.E = En;
+    const float down = pow2f(-En);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int tl = 16 * (k >> 1) + gid + 8 * (k & 1);
+        const float w = ws[k] * down;
+        const __half h = __float2half_rn(w);
+        const __half l2 = __float2half_rn(w - __half2float(h));
+        const int pos = mma_wpos(tl);
+        wtab[(2 * tig) * kMmaWRow + pos] = h;
+        wtab[(2 * tig + 1) * kMmaWRow + pos] = l2;
+    }
+    __syncwarp();
+    // ---- PV: channel tiles of 16, two k-steps of 16 tokens each ----
+    const int RV = mma_vrow_words(HG, HD);
+    const uint2 bw0 = *reinterpret_cast<const uint2*>(wtab + gid * kMmaWRow + 4 * tig);
+    const uint2 bw1 = *reinterpret_cast<const uint2*>(wtab + gid * kMmaWRow + 16 + 4 * tig);
+    const uint32_t* vrow = vw_s + (size_t)(ub + tig) * RV + kvl * DQ;
+#pragma unroll
+    for (int mh = 0; mh < DQ / 4; ++mh) {
+        float d[4][4];  // channel tiles 4mh..4mh+3
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            uint4 vv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                vv[i] = *reinterpret_cast<const uint4*>(vrow + (size_t)(16 * kk + 4 * i) * RV + 4 * mh);
+            const uint2 bw = kk == 0 ? bw0 : bw1;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t w0 = q == 0 ? vv[0].x : q == 1 ? vv[0].y : q == 2 ? vv[0].z : vv[0].w;
+                const uint32_t w1 = q == 0 ? vv[1].x : q == 1 ? vv[1].y : q == 2 ? vv[1].z : vv[1].w;
+                const uint32_t w2 = q == 0 ? vv[2].x : q == 1 ? vv[2].y : q == 2 ? vv[2].z : vv[2].w;
+                const uint32_t w3 = q == 0 ? vv[3].x : q == 1 ? vv[3].y : q == 2 ? vv[3].z : vv[3].w;
+                uint32_t a0, a1, a2, a3;
+                a_pair(w0, w1, sel, sft, a0, a1);
+                a_pair(w2, w3, sel, sft, a2, a3);
+                if (kk == 0) mma_f16_16816_z(d[q], a0, a1, a2, a3, bw.x, bw.y);
+                else mma_f16_16816(d[q], a0, a1, a2, a3, bw.x, bw.y);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            S.acc[4 * mh + q][0] = fmaf(S.acc[4 * mh + q][0], f, d[q][0] + d[q][1]);
+            S.acc[4 * mh + q][1] = fmaf(S.acc[4 * mh + q][1], f, d[q][2] + d[q][3]);
+        }
+    }
+    __syncwarp();
+}
+
+// Per-warp totals of the tensor-core unit for head tig: m, l and the output
+// channels 16mt+gid and 16mt+gid+8 (zero point folded back in).
+template <int HD>
+__device__ __forceinline__ void mma_finish(MmaState<HD>& S, float& m, float& l, float (&o)[HD / 16][2]) {
+    float L = S.l, SW = S.sws, SZ = S.spz;
+#pragma unroll
+    for (int x = 4; x <= 16; x <<= 1) {
+        L += __shfl_xor_sync(0xffffffffu, L, x);
+        SW += __shfl_xor_sync(0xffffffffu, SW, x);
+        SZ += __shfl_xor_sync(0xffffffffu, SZ, x);
+    }
+    const float up = pow2f(S.E);
+#pragma unroll
+    for (int mt = 0; mt < HD / 16; ++mt) {
+        o[mt][0] = (S.acc[mt][0] * up - 4.0f * SW) + SZ;
+        o[mt][1] = (S.acc[mt][1] * up - 4.0f * SW) + SZ;
+    }
+    m = S.m;
+    l = L;
+}
+
+}  // namespace tt
