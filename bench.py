@@ -32,6 +32,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import re
 import os
 import statistics
@@ -152,7 +153,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -162,7 +163,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
+
+    def wait_first(self, timeout=10.0):
+        """Block until nvidia-smi has printed a sample (it takes a moment to start)."""
+        t_end = time.monotonic() + timeout
+        while self.proc and not self.lines and time.monotonic() < t_end:
+            time.sleep(0.02)
 
     def __exit__(self, *a):
         if self.proc:
@@ -172,10 +179,14 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, t0=None, t1=None):
+        """Median SM clock, max clock and active throttle reasons of the samples
+        taken in [t0, t1] (monotonic seconds; all samples when not given)."""
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ts, ln in self.lines:
+            if t0 is not None and not (t0 <= ts <= t1):
+                continue
             p = [x.strip() for x in ln.split(",")]
             if len(p) < 9:
                 continue
@@ -281,37 +292,64 @@ def main():
     torch.cuda.synchronize()
     nq, nkv, hd = cfg["nq"], cfg["nkv"], cfg["hd"]
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(99 + rank)
+    gen.manual_seed(99)  # same inputs on every rank: the sharded step replicates the engines' state
     NSET = 4
     Qs = [torch.randn((L, nq * hd), generator=gen, device="cuda") for _ in range(NSET)]
     Ks = [torch.randn((L, nkv * hd), generator=gen, device="cuda") for _ in range(NSET)]
     Vs = [torch.randn((L, nkv * hd), generator=gen, device="cuda") for _ in range(NSET)]
     out = torch.empty((L, nq * hd), device="cuda")
 
+    # N > 1: one sequence sharded over the ranks (tt_engine_step_sharded_*,
+    # two NCCL all-gathers per step); N = 1: the batched step
+    step_fn = _C.engine_step_batched_sharded if world > 1 else _C.engine_step_batched
+
     def step(i):
         j = i % NSET
-        _C.engine_step_batched(engines, list(Qs[j]), list(Ks[j]), list(Vs[j]), list(out))
+        step_fn(engines, list(Qs[j]), list(Ks[j]), list(Vs[j]), list(out))
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    barrier()
-    # ---- timed region: device time, inputs resident ----
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        for i in range(args.warmup):
+            step(i)
         torch.cuda.synchronize()
         barrier()
+        # Clocks are sampled every 50 ms; the timed steps (a few ms) sit inside
+        # one continuous burst of the same steps, about 0.25 s of untimed steps
+        # on either side (same count on every rank), and the clock record is
+        # the samples taken during that burst.  The events bracket only the
+        # timed steps.
         e0.record(st)
-        for i in range(args.steps):
-            step(args.warmup + i)
+        step(args.warmup)
         e1.record(st)
         torch.cuda.synchronize()
+        one = torch.tensor([e0.elapsed_time(e1)], device="cuda")
+        if world > 1:
+            dist.all_reduce(one, op=dist.ReduceOp.MAX)
+        n_roll = int(min(600, max(10, math.ceil(250.0 / max(float(one.item()), 1e-3)))))
+        clk.wait_first()
         barrier()
+        k = args.warmup + 1
+        tb0 = time.monotonic()
+        for i in range(n_roll):
+            step(k + i)
+        k += n_roll
+        # ---- timed region: device time, inputs resident ----
+        e0.record(st)
+        for i in range(args.steps):
+            step(k + i)
+        e1.record(st)
+        k += args.steps
+        for i in range(n_roll):
+            step(k + i)
+        torch.cuda.synchronize()
+        tb1 = time.monotonic()
+        barrier()
+    clocks = clk.summary(tb0, tb1)
     ms = e0.elapsed_time(e1) / args.steps
     if world > 1:
         t = torch.tensor([ms], device="cuda")
@@ -340,7 +378,7 @@ def main():
         dQ.copy_(hQ, non_blocking=True)
         dK.copy_(hK, non_blocking=True)
         dV.copy_(hV, non_blocking=True)
-        _C.engine_step_batched(engines, list(dQ), list(dK), list(dV), list(out))
+        step_fn(engines, list(dQ), list(dK), list(dV), list(out))
         hO.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -371,7 +409,8 @@ def main():
         dense_tokens += dcount
         pbs_blocks += c["pbs_blocks_used"]
     part_ms = kt.partial_ms / max(kt.partial_launches, 1)
-    part_bytes = kv_bytes + q_out // 2  # reads every tier once + Q
+    # reads every tier once + Q; with N ranks each partial launch reads its 1/N share
+    part_bytes = kv_bytes // world + q_out // 2
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -387,7 +426,7 @@ def main():
         txt = open(os.path.join(ROOT, "profiles", "k_attn_partial_config2.md")).read()
         m = re.search(r"^dram_bytes_per_launch:\s*(\d+)", txt, re.M)
         if m and L == CFG2["layers"]:
-            traffic = int(m.group(1))
+            traffic = int(m.group(1)) // world  # each rank's launch reads its 1/N share
     except OSError:
         pass
 
@@ -422,7 +461,7 @@ def main():
                 "h2d_bytes_per_step": int(hQ.numel() * 4 + hK.numel() * 4 + hV.numel() * 4),
                 "d2h_bytes_per_step": int(hO.numel() * 4)},
         "gpu_launches": int(round(launches_per_step * args.steps)),
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         arrays = [host_layer_arrays(torch, engines[i], cfg) for i in range(4)]

@@ -220,6 +220,40 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
                                  const float* const* K_new, const float* const* V_new,
                                  float* const* attn_output, void* stream);
 
+/* Sequence-sharded decode step over `world` GPUs (one process per GPU).
+ * Every rank holds the same engines (same configuration, same inputs every
+ * step, so the same state); each rank attends a 1/world share of every
+ * engine's tokens: dense positions [D*r/w, D*(r+1)/w) and packed blocks
+ * [B*r/w, B*(r+1)/w).  Attention over a token set merges exactly through
+ * (max, sum, weighted sum) rows, the same decomposition the reference's softmax
+ * (fused_attn_avx2.cpp:245-284) allows; the reference itself has no multi-GPU
+ * path.  One step is three calls, stream-ordered, around two all-gathers that
+ * the caller performs with its collective library (NCCL, MPI, ...), all ranks
+ * in the same order:
+ *
+ *   tt_engine_sharded_slot_cap(engines, n, world, &slot)     (host only)
+ *   tt_engine_step_sharded_begin(..., xch_send)   maintenance + partial attention
+ *       xch_send: n * num_q_heads * (head_dim + 2) floats (device)
+ *   all-gather xch_send -> xch_all [world][n][num_q_heads][head_dim + 2]
+ *   tt_engine_step_sharded_merge(..., xch_all, attn_output, mw_send)
+ *       attn_output identical on every rank; mw_send: n * slot floats, this
+ *       rank's mean attention weights
+ *   all-gather mw_send -> mw_all [world][n][slot]
+ *   tt_engine_step_sharded_end(..., mw_all)       score feedback, all positions
+ *
+ * n <= 64.  slot must be at least what tt_engine_sharded_slot_cap returns
+ * just before the step.  A rank that skips a call leaves its engines out of
+ * step with the others. */
+tt_status tt_engine_sharded_slot_cap(tt_engine* const* engines, int n, int world, int* slot_cap);
+tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const float* const* Q,
+                                       const float* const* K_new, const float* const* V_new, int rank,
+                                       int world, int slot_cap, float* xch_send, void* stream);
+tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
+                                       const float* xch_all, float* const* attn_output, float* mw_send,
+                                       void* stream);
+tt_status tt_engine_step_sharded_end(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
+                                     const float* mw_all, void* stream);
+
 /* Replaces TriTierCacheEngine::prefill (cache_engine.cpp:271-395; binding
  * bindings.cpp:418-436): K_all/V_all [q_len, num_kv_heads, head_dim].
  * q_len < 0 -> TT_ERR_INVALID_ARGUMENT. */

@@ -1,0 +1,101 @@
+"""Sequence-sharded decode step across GPUs: one process per GPU, NCCL.
+
+Each rank holds the same engines, gets the same inputs and runs
+engine_step_batched_sharded (tt_engine_step_sharded_* around two NCCL
+all-gathers); it also keeps an unsharded copy of the engines on its own GPU.
+Checked every step: the output is bit-identical on all ranks and within the
+attention tolerance of the unsharded copy; score feedback within tolerance;
+counters equal.  As in the other engine tests, the unsharded copy's scores are
+written into the sharded engines after each step (score sync), so float
+rounding cannot route a token differently.  Runs only where at least two GPUs
+are visible; processes are bounded by a short process-group timeout and a
+join timeout.
+"""
+import multiprocessing as pymp
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-4, 1e-5
+
+
+def _worker(rank, world, port, q):
+    try:
+        import os
+        from datetime import timedelta
+        import torch.distributed as dist
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from tritiercache_b200 import _C
+        nq, nkv, hd, layers = 32, 8, 128, 2
+        cfg = (nq, nkv, hd, 4096, 4, 256, 0.05, 0.999, 32, 16, "fp16")
+        ref = [_C.TriTierCacheEngine(*cfg) for _ in range(layers)]
+        shd = [_C.TriTierCacheEngine(*cfg) for _ in range(layers)]
+        g = torch.Generator(device="cuda")
+        g.manual_seed(77)
+        for li in range(layers):
+            K = torch.randn(2500, nkv, hd, device="cuda", generator=g)
+            V = torch.randn(2500, nkv, hd, device="cuda", generator=g)
+            ref[li].prefill(K.data_ptr(), V.data_ptr(), 2500)
+            shd[li].prefill(K.data_ptr(), V.data_ptr(), 2500)
+        worst = 0.0
+        for step in range(32):
+            Q = [torch.randn(nq * hd, device="cuda", generator=g) for _ in range(layers)]
+            Kn = [torch.randn(nkv * hd, device="cuda", generator=g) for _ in range(layers)]
+            Vn = [torch.randn(nkv * hd, device="cuda", generator=g) for _ in range(layers)]
+            o_ref = [torch.empty(nq * hd, device="cuda") for _ in range(layers)]
+            o_shd = [torch.full((nq * hd,), float("nan"), device="cuda") for _ in range(layers)]
+            _C.engine_step_batched(ref, Q, Kn, Vn, o_ref)
+            _C.engine_step_batched_sharded(shd, Q, Kn, Vn, o_shd)
+            allo = [torch.empty(layers * nq * hd, device="cuda") for _ in range(world)]
+            dist.all_gather(allo, torch.cat(o_shd))
+            for r in range(1, world):
+                assert torch.equal(allo[r], allo[0]), (step, "outputs differ across ranks")
+            for li in range(layers):
+                err = (o_shd[li].double() - o_ref[li].double()).abs()
+                assert bool((err <= ATOL + RTOL * o_ref[li].double().abs()).all()), (step, li, float(err.max()))
+                worst = max(worst, float(err.max()))
+                gs, gr = shd[li].get_global_attn_scores().double(), ref[li].get_global_attn_scores().double()
+                assert bool(((gs - gr).abs() <= ATOL + RTOL * gr.abs()).all()), (step, li, "scores")
+                for k in ("total_processed_tokens", "hh_count", "pbs_blocks_used", "wr_count", "rw_head_index"):
+                    assert getattr(shd[li], k) == getattr(ref[li], k), (step, li, k)
+                shd[li].get_global_attn_scores().copy_(ref[li].get_global_attn_scores())
+                shd[li].get_HH_scores().copy_(ref[li].get_HH_scores())
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, None, worst))
+    except Exception as exc:
+        q.put((rank, repr(exc), None))
+
+
+def test_sharded_step_over_nccl():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs at least two GPUs")
+    world = 2
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = pymp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            rank, err, worst = q.get(timeout=300)
+            res[rank] = (err, worst)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert res[r][0] is None, (r, res[r][0])

@@ -467,3 +467,86 @@ def engine_step_batched(engines, Qs, Ks, Vs, outs) -> None:
     with torch.cuda.device(engines[0]._dev):
         check(lib().tt_engine_step_batched(hs, n, ptrs(Qs, "Q"), ptrs(Ks, "K_new"), ptrs(Vs, "V_new"),
                                            ptrs(outs, "attn_output"), _stream()), "engine_step_batched")
+
+
+class ShardedStep:
+    """The three calls of one sequence-sharded decode step for this rank
+    (tt_engine_step_sharded_begin / _merge / _end).  Every rank holds the same
+    engines and feeds them the same inputs; each attends a 1/world share of the
+    tokens.  Between the calls the caller all-gathers, in rank order, the
+    exchange rows (`begin` -> `merge`) and the mean weights (`merge` -> `end`).
+    No reference counterpart: the reference has no multi-GPU path."""
+
+    def __init__(self, engines, rank: int, world: int):
+        self.engines = list(engines)
+        self.rank, self.world = int(rank), int(world)
+        n = len(self.engines)
+        self._arr = C.c_void_p * n
+        self._hs = self._arr(*[e._h.value for e in self.engines])
+        self.nq, self.hd = self.engines[0].num_q_heads, self.engines[0].head_dim
+        self.xch_floats = n * self.nq * (self.hd + 2)   # per rank
+
+    def _ptrs(self, ts, name):
+        out = []
+        for t in ts:
+            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous()):
+                raise ValueError(f"sharded step: {name} entries must be contiguous CUDA tensors.")
+            out.append(t.data_ptr())
+        return self._arr(*out)
+
+    def slot_cap(self) -> int:
+        """Mean-weight slots per engine this rank needs for the next step."""
+        v = C.c_int()
+        check(lib().tt_engine_sharded_slot_cap(self._hs, len(self.engines), self.world, C.byref(v)), "slot_cap")
+        return v.value
+
+    def begin(self, Qs, Ks, Vs, xch_send: torch.Tensor, slot: int) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_step_sharded_begin(self._hs, len(self.engines), self._ptrs(Qs, "Q"),
+                                                     self._ptrs(Ks, "K_new"), self._ptrs(Vs, "V_new"), self.rank,
+                                                     self.world, slot, xch_send.data_ptr(), _stream()), "begin")
+
+    def merge(self, xch_all: torch.Tensor, outs, mw_send: torch.Tensor, slot: int) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_step_sharded_merge(self._hs, len(self.engines), self.rank, self.world, slot,
+                                                     xch_all.data_ptr(), self._ptrs(outs, "attn_output"),
+                                                     mw_send.data_ptr(), _stream()), "merge")
+
+    def end(self, mw_all: torch.Tensor, slot: int) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_step_sharded_end(self._hs, len(self.engines), self.rank, self.world, slot,
+                                                   mw_all.data_ptr(), _stream()), "end")
+
+
+_shard_buffers: dict = {}
+
+
+def engine_step_batched_sharded(engines, Qs, Ks, Vs, outs, group=None) -> None:
+    """engine_step_batched over the ranks of a torch.distributed process group
+    (NCCL, one process per GPU): every rank passes the same engines' handles
+    and the same inputs and receives the same outputs; each attends 1/world of
+    the tokens.  The exchange buffers are kept between calls."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = len(engines)
+    if not (len(Qs) == len(Ks) == len(Vs) == len(outs) == n):
+        raise ValueError("engine_step_batched_sharded: argument lengths differ.")
+    step = ShardedStep(engines, rank, world)
+    slot = step.slot_cap()
+    dev = Qs[0].device
+    key = (dev, n, step.nq, step.hd, world)
+    buf = _shard_buffers.get(key)
+    if buf is None or buf["slot"] < slot:
+        slot_alloc = max(slot, (buf["slot"] * 5 // 4) if buf else slot)
+        buf = {"slot": slot_alloc,
+               "xs": torch.empty(step.xch_floats, device=dev), "xa": torch.empty(world * step.xch_floats, device=dev),
+               "ms": torch.empty(n * slot_alloc, device=dev), "ma": torch.empty(world * n * slot_alloc, device=dev)}
+        _shard_buffers[key] = buf
+    slot = buf["slot"]
+    step.begin(Qs, Ks, Vs, buf["xs"], slot)
+    dist.all_gather_into_tensor(buf["xa"], buf["xs"], group=group)
+    step.merge(buf["xa"], outs, buf["ms"], slot)
+    dist.all_gather_into_tensor(buf["ma"], buf["ms"], group=group)
+    step.end(buf["ma"], slot)

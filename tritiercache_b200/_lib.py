@@ -61,7 +61,8 @@ EXPORTS = [
     "tt_engine_destroy", "tt_engine_step", "tt_engine_step_batched", "tt_engine_prefill",
     "tt_engine_get_counters", "tt_engine_get_buffer", "tt_engine_get_buffer_bytes",
     "tt_engine_device_bytes", "tt_engine_set_counters", "tt_profile_enable", "tt_profile_collect",
-    "tt_device_error", "tt_fused_attention_decode_noalloc",
+    "tt_device_error", "tt_fused_attention_decode_noalloc", "tt_engine_sharded_slot_cap",
+    "tt_engine_step_sharded_begin", "tt_engine_step_sharded_merge", "tt_engine_step_sharded_end",
 ]
 
 _lib = None
@@ -97,6 +98,11 @@ def _declare(L):
     L.tt_device_error.argtypes = [i, C.POINTER(i)]
     L.tt_fused_attention_decode_noalloc.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, vp, i,
                                                     i, vp]
+    pv = C.POINTER(vp)
+    L.tt_engine_sharded_slot_cap.argtypes = [pv, i, i, C.POINTER(i)]
+    L.tt_engine_step_sharded_begin.argtypes = [pv, i, pv, pv, pv, i, i, i, vp, vp]
+    L.tt_engine_step_sharded_merge.argtypes = [pv, i, i, i, i, vp, pv, vp, vp]
+    L.tt_engine_step_sharded_end.argtypes = [pv, i, i, i, i, vp, vp]
     for name in EXPORTS:
         if name not in ("tt_last_error", "tt_version"):
             getattr(L, name).restype = C.c_int

@@ -33,6 +33,30 @@ namespace tt {
 // ---------------------------------------------------------------------------
 // merge + mean weights + score feedback
 // ---------------------------------------------------------------------------
+// g[id] = decay * g[id] + w for the token at position `pos` (cache_engine.cpp:511-540):
+// sinks, heavy hitters (whose HH_scores copy follows), the recent ring and the
+// packed tier; ids outside [0, max_seq_len) are skipped.
+__device__ __forceinline__ void score_feedback(const JobDesc& J, const TierCounts& tc, int D, int pos, float w) {
+    long long id;
+    if (pos < tc.n0) {
+        id = pos;
+    } else if (pos < tc.n0 + tc.n1) {
+        const int i = pos - tc.n0;
+        id = J.hh_ids[i];
+        if (id >= 0 && id < J.msl) {
+            const float nv = fmaf(J.decay, J.g[id], w);
+            J.g[id] = nv;
+            J.hh_scores[i] = nv;
+        }
+        return;
+    } else if (pos < D) {
+        id = (long long)tc.total - tc.n2 + (pos - tc.n0 - tc.n1);
+    } else {
+        id = J.ids[pos - D];
+    }
+    if (id >= 0 && id < J.msl) J.g[id] = fmaf(J.decay, J.g[id], w);
+}
+
 __global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ AttnLaunch L) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ JobDesc Js;
@@ -130,27 +154,186 @@ __global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ At
         }
         const float w = sw / (float)nq;
         if (mw) mw[pos] = w;
-        if (J.g) {
-            long long id;
-            if (pos < tc.n0) {
-                id = pos;
-            } else if (pos < tc.n0 + tc.n1) {
-                const int i = pos - tc.n0;
-                id = J.hh_ids[i];
-                if (id >= 0 && id < J.msl) {
-                    const float nv = fmaf(J.decay, J.g[id], w);
-                    J.g[id] = nv;
-                    J.hh_scores[i] = nv;
-                }
-                continue;
-            } else if (pos < D) {
-                id = (long long)tc.total - tc.n2 + (pos - tc.n0 - tc.n1);
-            } else {
-                id = J.ids[pos - D];
+        if (J.g) score_feedback(J, tc, D, pos, w);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// sequence-sharded attention (see launch_sharded_* in tt_attn.cuh)
+// ---------------------------------------------------------------------------
+// Sum of the positions' weights over heads / nq, as in k_attn_finalize.
+__device__ __forceinline__ float mean_weight(const JobDesc& J, const float* Ms, const float* IL, int nq, int pos) {
+    const float* sc = J.scores;
+    const size_t stride = (size_t)J.score_stride;
+    float sw = 0.f;
+    int h = 0;
+    for (; h + 8 <= nq; h += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (v[k] != -INFINITY) sw = fmaf(exp2f(v[k] - Ms[h + k]), IL[h + k], sw);
+    }
+    for (; h < nq; ++h) {
+        const float v = sc[(size_t)h * stride + pos];
+        if (v != -INFINITY) sw = fmaf(exp2f(v - Ms[h]), IL[h], sw);
+    }
+    return sw / (float)nq;
+}
+
+// Position of local index i of a rank's share (dense positions first).
+__device__ __forceinline__ int shard_pos(const ShardRange& R, int D, int i) {
+    const int nd = R.dhi - R.dlo;
+    return i < nd ? R.dlo + i : D + R.plo + (i - nd);
+}
+
+// Phase 1 epilogue: this rank's chunk partials -> one (m, l, acc) row per head.
+// grid (nq, njobs); dynamic shared memory: nd + np floats.
+__global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant__ AttnLaunch L, float* xch) {
+    extern __shared__ float wts[];
+    __shared__ JobDesc Js;
+    __shared__ TierCounts Ts;
+    __shared__ float red[NW];
+    __shared__ float Mh, Lh;
+    const int job = blockIdx.y, h = blockIdx.x;
+    if (threadIdx.x == 0) {
+        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
+        Ts = resolve_counts(Js);
+    }
+    __syncthreads();
+    const JobDesc& J = Js;
+    const TierCounts tc = Ts;
+    const int nq = J.nq, HD = J.hd;
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
+    const int nd_act = ceil_div(R.dhi - R.dlo, L.DC), np_act = ceil_div(R.phi - R.plo, L.PC);
+    const int nch = nd_act + np_act;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto chunk_index = [&](int i) { return i < nd_act ? i : L.nd + (i - nd_act); };
+
+    float M = -INFINITY;
+    for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
+    M = warp_max(M);
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = red[0];
+        for (int w = 1; w < NW; ++w) m = fmaxf(m, red[w]);
+        Mh = m;
+    }
+    __syncthreads();
+    M = Mh;
+    float S = 0.f;
+    for (int i = threadIdx.x; i < nch; i += NT) {
+        const size_t pi = ((size_t)chunk_index(i) * nq + h) * 2;
+        const float mi = J.part_ml[pi];
+        const float w = (M == -INFINITY || mi == -INFINITY) ? 0.f : exp2f(mi - M);
+        wts[i] = w;
+        S = fmaf(J.part_ml[pi + 1], w, S);
+    }
+    S = warp_sum(S);
+    __syncthreads();
+    if (lane == 0) red[warp] = S;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < NW; ++w) t += red[w];
+        Lh = t;
+    }
+    __syncthreads();
+    float* dst = xch + ((size_t)job * nq + h) * (HD + 2);
+    for (int c = threadIdx.x; c < HD; c += NT) {
+        float o = 0.f;
+        for (int i = 0; i < nch; ++i) o = fmaf(J.part_acc[((size_t)chunk_index(i) * nq + h) * HD + c], wts[i], o);
+        dst[2 + c] = o;
+    }
+    if (threadIdx.x == 0) {
+        dst[0] = M;
+        dst[1] = Lh;
+    }
+}
+
+// Phase 2: every rank's rows -> output (ranks merged in order 0..world-1, so
+// all ranks produce the same bits) and this rank's mean weights.
+// grid (gx, njobs); dynamic shared memory: 2 nq floats.
+__global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ AttnLaunch L, const float* xch_all,
+                                                    float* mw_send, int slot_cap) {
+    extern __shared__ float sm[];
+    __shared__ JobDesc Js;
+    __shared__ TierCounts Ts;
+    const int job = blockIdx.y;
+    if (threadIdx.x == 0) {
+        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
+        Ts = resolve_counts(Js);
+    }
+    __syncthreads();
+    const JobDesc& J = Js;
+    const TierCounts tc = Ts;
+    const int nq = J.nq, HD = J.hd, P = L.world;
+    float* Ms = sm;
+    float* IL = sm + nq;
+    const size_t row = (size_t)HD + 2, rstride = (size_t)L.njobs * nq * row;
+    const float* base = xch_all + (size_t)job * nq * row;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int h = warp; h < nq; h += NW) {
+        float M = -INFINITY;
+        for (int p = lane; p < P; p += 32) M = fmaxf(M, base[p * rstride + h * row]);
+        M = warp_max(M);
+        float S = 0.f;
+        if (M != -INFINITY)
+            for (int p = lane; p < P; p += 32) {
+                const float mp = base[p * rstride + h * row];
+                if (mp != -INFINITY) S = fmaf(base[p * rstride + h * row + 1], exp2f(mp - M), S);
             }
-            if (id >= 0 && id < J.msl) J.g[id] = fmaf(J.decay, J.g[id], w);
+        S = warp_sum(S);
+        if (lane == 0) {
+            Ms[h] = M;
+            IL[h] = 1.0f / (S > 0.f ? S : 1.0f);
         }
     }
+    __syncthreads();
+    float* out = L.out[job];
+    for (int h = blockIdx.x; h < nq; h += gridDim.x) {
+        const float M = Ms[h], inv = IL[h];
+        for (int c = threadIdx.x; c < HD; c += NT) {
+            float o = 0.f;
+            for (int p = 0; p < P; ++p) {
+                const float mp = base[p * rstride + h * row];
+                if (M != -INFINITY && mp != -INFINITY)
+                    o = fmaf(base[p * rstride + h * row + 2 + c], exp2f(mp - M) * inv, o);
+            }
+            out[(size_t)h * HD + c] = o;
+        }
+    }
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, P);
+    const int n_loc = min(slot_cap, (R.dhi - R.dlo) + (R.phi - R.plo));  // the host checked n_loc <= slot_cap
+    for (int i = blockIdx.x * NT + threadIdx.x; i < n_loc; i += gridDim.x * NT)
+        mw_send[(size_t)job * slot_cap + i] = mean_weight(J, Ms, IL, nq, shard_pos(R, D, i));
+}
+
+// Phase 3: every rank's mean weights -> score feedback for all positions.
+// grid (ceil(slot_cap / NT), njobs, world).
+__global__ void __launch_bounds__(NT) k_shard_feedback(const __grid_constant__ AttnLaunch L, const float* mw_all,
+                                                       int slot_cap) {
+    __shared__ JobDesc Js;
+    __shared__ TierCounts Ts;
+    const int job = blockIdx.y, p = blockIdx.z;
+    if (threadIdx.x == 0) {
+        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
+        Ts = resolve_counts(Js);
+    }
+    __syncthreads();
+    const JobDesc& J = Js;
+    const TierCounts tc = Ts;
+    if (!J.g) return;
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const ShardRange R = shard_range(D, tc.nblk, J.grp, p, L.world);
+    const int n_loc = (R.dhi - R.dlo) + (R.phi - R.plo);
+    const int i = blockIdx.x * NT + threadIdx.x;
+    if (i >= n_loc || i >= slot_cap) return;
+    score_feedback(J, tc, D, shard_pos(R, D, i), mw_all[((size_t)p * L.njobs + job) * slot_cap + i]);
 }
 
 // ---------------------------------------------------------------------------
@@ -246,19 +429,51 @@ static tt_status launch_partial_hd(const AttnLaunch& L, cudaStream_t st) {
     return set_error(TT_ERR_UNSUPPORTED, "unsupported GQA ratio");
 }
 
+static tt_status launch_partial_any(const AttnLaunch& L, cudaStream_t st) {
+    if (L.nd + L.np == 0) return TT_OK;
+    switch (L.inline_job.hd) {  // callers always fill inline_job.hd/nq (also for engine batches)
+        case 16: return launch_partial_hd<16>(L, st);
+        case 32: return launch_partial_hd<32>(L, st);
+        case 64: return launch_partial_hd<64>(L, st);
+        case 128: return launch_partial_hd<128>(L, st);
+        case 256: return launch_partial_hd<256>(L, st);
+        default: return set_error(TT_ERR_UNSUPPORTED, "unsupported head_dim");
+    }
+}
+
+tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t st) {
+    tt_status s = launch_partial_any(L, st);
+    if (s != TT_OK) return s;
+    dim3 grid(L.inline_job.nq, L.njobs);
+    const int ps = prof_begin(2, st);  // the sharded epilogue kernels count as finalize
+    k_shard_local_merge<<<grid, NT, (size_t)(L.nd + L.np + 1) * sizeof(float), st>>>(L, xch);
+    prof_end(ps, st);
+    return check_launch("k_shard_local_merge");
+}
+
+tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, float* mw_send, int slot_cap,
+                               cudaStream_t st) {
+    const int gx = std::max(L.inline_job.nq, ceil_div(slot_cap, 4 * NT));
+    dim3 grid(gx, L.njobs);
+    const int ps = prof_begin(2, st);
+    k_shard_merge<<<grid, NT, (size_t)2 * L.inline_job.nq * sizeof(float), st>>>(L, xch_all, mw_send, slot_cap);
+    prof_end(ps, st);
+    return check_launch("k_shard_merge");
+}
+
+tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int slot_cap, cudaStream_t st) {
+    dim3 grid(std::max(1, ceil_div(slot_cap, NT)), L.njobs, L.world);
+    const int ps = prof_begin(2, st);
+    k_shard_feedback<<<grid, NT, 0, st>>>(L, mw_all, slot_cap);
+    prof_end(ps, st);
+    return check_launch("k_shard_feedback");
+}
+
 // L.inline_job.hd / .nq must be set for engine batches too (they select the
 // kernel instantiation and the finalize shared memory).
 tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
-    if (L.nd + L.np > 0) {
-        tt_status s;
-        switch (L.inline_job.hd) {  // callers always fill inline_job.hd/nq (also for engine batches)
-            case 16: s = launch_partial_hd<16>(L, st); break;
-            case 32: s = launch_partial_hd<32>(L, st); break;
-            case 64: s = launch_partial_hd<64>(L, st); break;
-            case 128: s = launch_partial_hd<128>(L, st); break;
-            case 256: s = launch_partial_hd<256>(L, st); break;
-            default: return set_error(TT_ERR_UNSUPPORTED, "unsupported head_dim");
-        }
+    {
+        tt_status s = launch_partial_any(L, st);
         if (s != TT_OK) return s;
     }
     dim3 grid(L.nfin, L.njobs);

@@ -88,6 +88,7 @@ struct AttnLaunch {
     int FT;       // tokens per finalize CTA
     int nfin;     // finalize CTAs per job
     int meta_bytes;  // largest PBS metadata element of the batch (2 or 4): sizes the staging buffers
+    int rank, world; // sequence sharding: this launch attends only its share (world <= 1: everything)
     const JobDesc* jobs[kMaxBatch];  // device descriptor per job (engines) or nullptr
     JobDesc inline_job;              // stand-alone job (jobs[0] == nullptr, njobs == 1)
     const float* Q[kMaxBatch];
@@ -99,9 +100,42 @@ struct AttnLaunch {
 // capacities are dense_cap / pbs_tok_cap.  Returns TT_ERR_UNSUPPORTED for
 // shapes the kernels are not built for.
 tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, int pbs_tok_cap);
+
+// The tokens one rank of `world` attends: dense positions [dlo, dhi) and
+// packed token offsets [plo, phi) (whole blocks).  Every rank derives the same
+// split from the same (replicated) counters.
+struct ShardRange {
+    int dlo, dhi, plo, phi;
+};
+__host__ __device__ __forceinline__ ShardRange shard_range(int D, int nblk, int grp, int rank, int world) {
+    ShardRange r;
+    if (world <= 1) {
+        r.dlo = 0; r.dhi = D; r.plo = 0; r.phi = nblk * grp;
+    } else {
+        r.dlo = (int)((long long)D * rank / world);
+        r.dhi = (int)((long long)D * (rank + 1) / world);
+        r.plo = (int)((long long)nblk * rank / world) * grp;
+        r.phi = (int)((long long)nblk * (rank + 1) / world) * grp;
+    }
+    return r;
+}
 // Scratch a job needs for a given plan: chunk slots and score stride.
 int attn_max_chunks(int dense_cap, int pbs_tok_cap);
 // Launches the partial and finalize kernels on `stream`.
 tt_status launch_attention(const AttnLaunch& L, cudaStream_t stream);
+
+// Sequence-sharded attention, three stream-ordered phases around two
+// all-gathers done by the caller (L.rank / L.world set, L.mw unused):
+//  1. partial attention over this rank's share, merged into one
+//     (m, l, acc[hd]) row per (job, head): xch[job][h][hd + 2];
+//  2. given every rank's rows (xch_all[world][njobs][nq][hd + 2]): the output
+//     (same arithmetic and order on every rank) and the mean attention weights
+//     of this rank's positions: mw_send[job][slot_cap];
+//  3. given every rank's weights (mw_all[world][njobs][slot_cap]): score
+//     feedback for all positions, identical on every rank.
+tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t stream);
+tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, float* mw_send, int slot_cap,
+                               cudaStream_t stream);
+tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int slot_cap, cudaStream_t stream);
 
 }  // namespace tt

@@ -600,14 +600,18 @@ tt_status tt_engine_destroy(tt_engine* e) {
     return TT_OK;
 }
 
-tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* const* Q, const float* const* K_new,
-                                 const float* const* V_new, float* const* attn_output, void* stream) {
-    if (n <= 0) return TT_OK;
-    if (!engines || !Q || !K_new || !V_new || !attn_output) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+}  // extern "C"
+
+namespace {
+
+// Argument checks shared by the batched and the sharded step.
+tt_status validate_step(tt_engine* const* engines, int n, const float* const* Q, const float* const* K_new,
+                        const float* const* V_new) {
+    if (!engines || !Q || !K_new || !V_new) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
     for (int i = 0; i < n; ++i) {
         tt_status s = validate(engines[i]);
         if (s != TT_OK) return s;
-        if (!Q[i] || !K_new[i] || !V_new[i] || !attn_output[i])
+        if (!Q[i] || !K_new[i] || !V_new[i])
             return set_error(TT_ERR_INVALID_ARGUMENT, "Q, K_new, V_new and attn_output must not be NULL.");
         const tt_engine_config& a = engines[i]->cfg;
         const tt_engine_config& b = engines[0]->cfg;
@@ -617,71 +621,212 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
         if (((uintptr_t)Q[i] & 15) || ((uintptr_t)K_new[i] & 15) || ((uintptr_t)V_new[i] & 15))
             return set_error(TT_ERR_INVALID_ARGUMENT, "Q, K_new and V_new must be 16-byte aligned.");
     }
+    return TT_OK;
+}
+
+// Does this step evict a ring token (host mirror of the counters)?
+bool step_evicts(const tt_engine* e) { return !(e->h_s < e->cfg.sink_size) && !(e->h_rw < e->cfg.rw_size); }
+
+// Upper bound on the packed blocks after this step's maintenance.
+long long step_block_bound(const tt_engine* e) {
+    return (e->h_wr_pbs_ub + (step_evicts(e) ? 1 : 0)) / e->chunk;
+}
+
+// Maintenance of engines[0..m) in one launch; returns the dense and packed
+// token capacities the attention launch must cover.
+tt_status maintain_batch(tt_engine* const* engines, int m, const float* const* K_new, const float* const* V_new,
+                         cudaStream_t st, int& dcap, int& pcap) {
+    MaintBatch mb;
+    memset(&mb, 0, sizeof(mb));
+    mb.n = m;
+    dcap = 0;
+    pcap = 0;
+    for (int i = 0; i < m; ++i) {
+        tt_engine* e = engines[i];
+        if (step_evicts(e)) {
+            tt_status s = ensure_capacity(e, e->h_wr_pbs_ub + 1);
+            if (s != TT_OK) return s;
+        }
+        mb.d[i] = reinterpret_cast<const MaintDesc*>(e->maint_dev);
+        mb.K[i] = K_new[i];
+        mb.V[i] = V_new[i];
+        dcap = std::max(dcap, dense_cap(e));
+        pcap = std::max<long long>(pcap, std::min<long long>(step_block_bound(e), e->pbs_cap) * e->chunk);
+    }
+    const int ps = prof_begin(0, st);
+    k_engine_maintain<<<m, MT, 0, st>>>(mb);
+    prof_end(ps, st);
+    return check_launch("k_engine_maintain");
+}
+
+// Attention launch description for engines[0..m) (jobs, Q, outputs).
+void fill_launch(AttnLaunch& L, tt_engine* const* engines, int m, const float* const* Q, float* const* out) {
+    L.njobs = m;
+    const tt_engine_config& c0 = engines[0]->cfg;
+    L.inline_job.hd = c0.head_dim;
+    L.inline_job.nq = c0.num_q_heads;
+    L.meta_bytes = 2;
+    for (int i = 0; i < m; ++i)
+        if (!engines[i]->cfg.meta_fp16) L.meta_bytes = 4;
+    for (int i = 0; i < m; ++i) {
+        L.jobs[i] = engines[i]->job_dev;
+        L.Q[i] = Q ? Q[i] : nullptr;
+        L.out[i] = out ? out[i] : nullptr;
+        L.mw[i] = nullptr;
+    }
+}
+
+// Host mirrors of the counters after one step of engines[0..m).
+void advance_mirrors(tt_engine* const* engines, int m, cudaStream_t st) {
+    for (int i = 0; i < m; ++i) {
+        tt_engine* e = engines[i];
+        if (e->h_s < e->cfg.sink_size) {
+            e->h_s++;
+        } else if (e->h_rw < e->cfg.rw_size) {
+            e->h_rw++;
+        } else {
+            e->h_rw_head = (e->h_rw_head + 1) % e->cfg.rw_size;
+            e->h_evictions++;
+            e->h_wr_pbs_ub++;
+        }
+        e->h_total++;
+        e->last_stream = st;
+    }
+}
+
+// Positions one rank of `world` may hold in the next step (slot capacity).
+long long shard_slot_need(const tt_engine* e, int world) {
+    return (long long)ceil_div(dense_cap(e), world) + (step_block_bound(e) + world - 1) / world * e->chunk;
+}
+
+tt_status validate_shard_args(tt_engine* const* engines, int n, int rank, int world, int slot_cap) {
+    if (!engines) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if (n > kMaxBatch) return set_error(TT_ERR_INVALID_ARGUMENT, "a sharded step takes at most %d engines.", kMaxBatch);
+    if (world < 1 || rank < 0 || rank >= world)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "rank %d / world %d out of range.", rank, world);
+    if (slot_cap < 0) return set_error(TT_ERR_INVALID_ARGUMENT, "slot_cap must be non-negative.");
+    for (int i = 0; i < n; ++i) {
+        tt_status s = validate(engines[i]);
+        if (s != TT_OK) return s;
+    }
+    return TT_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* const* Q, const float* const* K_new,
+                                 const float* const* V_new, float* const* attn_output, void* stream) {
+    if (n <= 0) return TT_OK;
+    if (!attn_output) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_status s = validate_step(engines, n, Q, K_new, V_new);
+    if (s != TT_OK) return s;
+    for (int i = 0; i < n; ++i)
+        if (!attn_output[i])
+            return set_error(TT_ERR_INVALID_ARGUMENT, "Q, K_new, V_new and attn_output must not be NULL.");
     DeviceGuard dg(engines[0]->cfg.device);
     cudaStream_t st = (cudaStream_t)stream;
     for (int base = 0; base < n; base += kMaxBatch) {
         const int m = std::min(kMaxBatch, n - base);
-        MaintBatch mb;
-        memset(&mb, 0, sizeof(mb));
-        mb.n = m;
         int dcap = 0, pcap = 0;
-        for (int i = 0; i < m; ++i) {
-            tt_engine* e = engines[base + i];
-            // host mirrors: does this step evict?
-            const bool evicts = !(e->h_s < e->cfg.sink_size) && !(e->h_rw < e->cfg.rw_size);
-            if (evicts) {
-                tt_status s = ensure_capacity(e, e->h_wr_pbs_ub + 1);
-                if (s != TT_OK) return s;
-            }
-            mb.d[i] = reinterpret_cast<const MaintDesc*>(e->maint_dev);
-            mb.K[i] = K_new[base + i];
-            mb.V[i] = V_new[base + i];
-            dcap = std::max(dcap, dense_cap(e));
-            const long long ub_blocks = (e->h_wr_pbs_ub + (evicts ? 1 : 0)) / e->chunk;
-            pcap = std::max<long long>(pcap, std::min<long long>(ub_blocks, e->pbs_cap) * e->chunk);
-        }
-        const int ps = prof_begin(0, st);
-        k_engine_maintain<<<m, MT, 0, st>>>(mb);
-        prof_end(ps, st);
-        tt_status s = check_launch("k_engine_maintain");
+        s = maintain_batch(engines + base, m, K_new + base, V_new + base, st, dcap, pcap);
         if (s != TT_OK) return s;
-
         AttnLaunch L;
         memset(&L, 0, sizeof(L));
         L.njobs = m;
         const tt_engine_config& c0 = engines[base]->cfg;
         s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, dcap, pcap);
         if (s != TT_OK) return s;
-        L.inline_job.hd = c0.head_dim;
-        L.inline_job.nq = c0.num_q_heads;
-        L.meta_bytes = 2;
-        for (int i = 0; i < m; ++i)
-            if (!engines[base + i]->cfg.meta_fp16) L.meta_bytes = 4;
-        for (int i = 0; i < m; ++i) {
-            tt_engine* e = engines[base + i];
-            L.jobs[i] = e->job_dev;
-            L.Q[i] = Q[base + i];
-            L.out[i] = attn_output[base + i];
-            L.mw[i] = nullptr;
-        }
+        fill_launch(L, engines + base, m, Q + base, attn_output + base);
         s = launch_attention(L, st);
         if (s != TT_OK) return s;
-        for (int i = 0; i < m; ++i) {
-            tt_engine* e = engines[base + i];
-            if (e->h_s < e->cfg.sink_size) {
-                e->h_s++;
-            } else if (e->h_rw < e->cfg.rw_size) {
-                e->h_rw++;
-            } else {
-                e->h_rw_head = (e->h_rw_head + 1) % e->cfg.rw_size;
-                e->h_evictions++;
-                e->h_wr_pbs_ub++;
-            }
-            e->h_total++;
-            e->last_stream = st;
-        }
+        advance_mirrors(engines + base, m, st);
     }
     return TT_OK;
+}
+
+tt_status tt_engine_sharded_slot_cap(tt_engine* const* engines, int n, int world, int* slot_cap) {
+    if (!engines || !slot_cap) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if (world < 1) return set_error(TT_ERR_INVALID_ARGUMENT, "world must be at least 1.");
+    long long need = 0;
+    for (int i = 0; i < n; ++i) {
+        tt_status s = validate(engines[i]);
+        if (s != TT_OK) return s;
+        need = std::max(need, shard_slot_need(engines[i], world));
+    }
+    if (need > (1LL << 30)) return set_error(TT_ERR_INVALID_ARGUMENT, "slot capacity overflow.");
+    *slot_cap = (int)need;
+    return TT_OK;
+}
+
+tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const float* const* Q,
+                                       const float* const* K_new, const float* const* V_new, int rank, int world,
+                                       int slot_cap, float* xch_send, void* stream) {
+    if (n <= 0) return TT_OK;
+    tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
+    if (s != TT_OK) return s;
+    s = validate_step(engines, n, Q, K_new, V_new);
+    if (s != TT_OK) return s;
+    if (!xch_send) return set_error(TT_ERR_INVALID_ARGUMENT, "xch_send must not be NULL.");
+    for (int i = 0; i < n; ++i)
+        if (shard_slot_need(engines[i], world) > slot_cap)
+            return set_error(TT_ERR_INVALID_ARGUMENT,
+                             "slot_cap %d is below this step's need (tt_engine_sharded_slot_cap).", slot_cap);
+    DeviceGuard dg(engines[0]->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int dcap = 0, pcap = 0;
+    s = maintain_batch(engines, n, K_new, V_new, st, dcap, pcap);
+    if (s != TT_OK) return s;
+    AttnLaunch L;
+    memset(&L, 0, sizeof(L));
+    L.njobs = n;
+    const tt_engine_config& c0 = engines[0]->cfg;
+    // this rank's share: ceil(D / world) dense positions, ceil(blocks / world) blocks
+    const int chunk = engines[0]->chunk;
+    const int pcap_r = ceil_div(ceil_div(pcap, chunk), world) * chunk;
+    s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, ceil_div(dcap, world), pcap_r);
+    if (s != TT_OK) return s;
+    fill_launch(L, engines, n, Q, nullptr);
+    L.rank = rank;
+    L.world = world;
+    s = launch_sharded_partial(L, xch_send, st);
+    if (s != TT_OK) return s;
+    advance_mirrors(engines, n, st);
+    return TT_OK;
+}
+
+tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
+                                       const float* xch_all, float* const* attn_output, float* mw_send,
+                                       void* stream) {
+    if (n <= 0) return TT_OK;
+    tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
+    if (s != TT_OK) return s;
+    if (!xch_all || !attn_output || !mw_send) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    for (int i = 0; i < n; ++i)
+        if (!attn_output[i]) return set_error(TT_ERR_INVALID_ARGUMENT, "attn_output must not be NULL.");
+    DeviceGuard dg(engines[0]->cfg.device);
+    AttnLaunch L;
+    memset(&L, 0, sizeof(L));
+    fill_launch(L, engines, n, nullptr, attn_output);
+    L.rank = rank;
+    L.world = world;
+    return launch_sharded_merge(L, xch_all, mw_send, slot_cap, (cudaStream_t)stream);
+}
+
+tt_status tt_engine_step_sharded_end(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
+                                     const float* mw_all, void* stream) {
+    if (n <= 0) return TT_OK;
+    tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
+    if (s != TT_OK) return s;
+    if (!mw_all) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    DeviceGuard dg(engines[0]->cfg.device);
+    AttnLaunch L;
+    memset(&L, 0, sizeof(L));
+    fill_launch(L, engines, n, nullptr, nullptr);
+    L.rank = rank;
+    L.world = world;
+    return launch_sharded_feedback(L, mw_all, slot_cap, (cudaStream_t)stream);
 }
 
 tt_status tt_engine_step(tt_engine* e, const float* Q, const float* K_new, const float* V_new, float* attn_output,

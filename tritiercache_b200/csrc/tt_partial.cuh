@@ -726,15 +726,16 @@ __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __gr
     const JobDesc& J = Js;
     const TierCounts tc = Ts;
     const int D = tc.n0 + tc.n1 + tc.n2;
-    const int ntok = tc.nblk * J.grp;
+    // this launch's share of the positions (all of them unless sharded)
+    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
     const bool is_dense = (int)blockIdx.x < L.nd;
     int t0, t1;
     if (is_dense) {
-        t0 = blockIdx.x * L.DC;
-        t1 = min(D, t0 + L.DC);
+        t0 = R.dlo + blockIdx.x * L.DC;
+        t1 = min(R.dhi, t0 + L.DC);
     } else {
-        t0 = (blockIdx.x - L.nd) * L.PC;
-        t1 = min(ntok, t0 + L.PC);
+        t0 = R.plo + (blockIdx.x - L.nd) * L.PC;
+        t1 = min(R.phi, t0 + L.PC);
     }
     if (t0 >= t1) return;
 

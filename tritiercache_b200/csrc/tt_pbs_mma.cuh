@@ -167,7 +167,7 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, in
                                              const MmaQ<HD>& Q, unsigned char* wa, MmaState<HD>& S) {
     static_assert((HD == 64 || HD == 128) && GM <= 4, "tensor-core unit shape");
     static_assert(MmaWarpArea<HD>::bytes <= WarpArea<HD, GM, true>::bytes, "weight table fits the warp area");
-    constexpr int KS = HD / 16, MT = HD / 16, DQ = HD / 16;
+    constexpr int KS = HD / 16, DQ = HD / 16;
     const int gid = lane >> 2, tig = lane & 3;
     const int sft = 2 * (gid & 3);
     const uint32_t sel = 0x6420u + 0x1111u * (uint32_t)(gid >> 2);
