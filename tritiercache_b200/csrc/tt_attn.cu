@@ -386,13 +386,13 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
 
 template <int HD, int GM, bool MMA>
 static tt_status launch_partial_t(const AttnLaunch& L, cudaStream_t st) {
-    const size_t sm = partial_smem_bytes<HD, GM, MMA>(L.HG, L.meta_bytes);
+    const size_t sm = kernel_smem_bytes<HD, GM, MMA>(L.HG, L.meta_bytes);
     static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
         size_t mx = 0;
-        for (int hg = 1; hg <= 8; hg *= 2) mx = std::max(mx, partial_smem_bytes<HD, GM, MMA>(hg, 4));
+        for (int hg = 1; hg <= 8; ++hg) mx = std::max(mx, kernel_smem_bytes<HD, GM, MMA>(hg, 4));
         cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD, GM, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)mx);
         if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(k_attn_partial)");
@@ -406,12 +406,12 @@ static tt_status launch_partial_t(const AttnLaunch& L, cudaStream_t st) {
 }
 
 // Packed chunks run on the tensor cores (mma.sync f16) for head_dim 64 / 128,
-// up to 4 query heads per kv head and fp16 metadata in every job of the
-// batch; other shapes keep the SIMT unit.
+// up to 4 query heads per kv head, an even number of kv heads and fp16
+// metadata in every job of the batch; other shapes keep the SIMT unit.
 template <int HD, int GM>
 static tt_status launch_partial_g(const AttnLaunch& L, cudaStream_t st) {
     if constexpr ((HD == 64 || HD == 128) && GM <= 4) {
-        if (L.meta_bytes == 2) return launch_partial_t<HD, GM, true>(L, st);
+        if (L.meta_bytes == 2 && (L.HG * L.nhg) % 2 == 0) return launch_partial_t<HD, GM, true>(L, st);
     }
     return launch_partial_t<HD, GM, false>(L, st);
 }

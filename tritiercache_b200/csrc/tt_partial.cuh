@@ -24,7 +24,6 @@ namespace tt {
 constexpr int NT = 256;
 constexpr int NW = NT / TT_WARP;
 constexpr int NSTAGE = 2;    // stages in flight, SIMT packed unit
-constexpr int NSTAGE_M = 3;  // stages in flight, tensor-core packed unit
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ int g_device_error = 0;  // first device-side error code (tt_status), cleared by the host
@@ -97,23 +96,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase)
         if (mbar_try_wait(bar, phase)) return true;
     return false;
 }
-// 16-byte asynchronous copy global -> shared (L2 only); completion is reported
-// to an mbarrier by cp_async_arrive.
+// 16-byte asynchronous copy global -> shared (L2 only; cp.async groups).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-// One arrival on `bar` once this thread's earlier cp.async copies have landed
-// (.noinc: the barrier's expected count already includes it).
-__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-// Bounded wait that also gives up once *abort is set (checked every 256 polls).
-__device__ __forceinline__ bool mbar_wait_abortable(uint64_t* bar, uint32_t phase, volatile int* abort) {
-    for (int i = 0; i < (1 << 20); ++i) {
-        if (mbar_try_wait(bar, phase)) return true;
-        if ((i & 255) == 255 && *abort) return false;
-    }
-    return false;
 }
 // 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
 __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -135,24 +120,23 @@ __host__ __device__ __forceinline__ int stage_tokens(int HG) { return 32 * (NW /
 struct StageLayout {
     int kw, ks, kz, vw, vs, vz, ids, bytes;
 };
-// vpad: V words of a token start a row of HG*DQ + 4 words (tensor-core unit)
-__host__ __device__ __forceinline__ StageLayout stage_layout(int HD, int mb, int HG = 8, bool vpad = false) {
+__host__ __device__ __forceinline__ StageLayout stage_layout(int HD, int mb, int HG = 8) {
     StageLayout s;
     int o = 0;
     s.kw = o; o += 16 * HD * 4;              // [ST/16 rows][HG][HD] words   (rows*HG = 16)
     s.ks = o; o += align_up(16 * HD * mb, 16);  // [blocks][HG][HD]        (blocks*HG <= 16)
     s.kz = o; o += align_up(16 * HD * mb, 16);
     s.vw = o;                                // [ST][HG][DQ] (+ pad per token)
-    o += vpad ? stage_tokens(HG) * (HG * (HD / 16) + 4) * 4 : 256 * (HD / 16) * 4;
+    o += 256 * (HD / 16) * 4;
     s.vs = o; o += align_up(256 * mb, 16);   // [ST][HG]
     s.vz = o; o += align_up(256 * mb, 16);
-    s.ids = o; o += (vpad ? stage_tokens(HG) : 256) * 8;  // [ST] (ST <= 256)
+    s.ids = o; o += 256 * 8;                 // [ST] (ST <= 256)
     s.bytes = align_up(o, 128);
     return s;
 }
 
-// MMA: the kernel whose packed chunks use the tensor-core unit, which needs
-// only a 768-byte weight table per warp (no q*scale table).
+// MMA: the kernel whose packed chunks use the tensor-core unit (its warp
+// areas are MmaWarpArea; dense units only need the dense tables here).
 template <int HD, int GM, bool MMA = false>
 struct WarpArea {
     // packed units: q*scale table [half][HD][GM]; dense units reuse the same
@@ -165,14 +149,13 @@ struct WarpArea {
     static constexpr int sc = 0;
     static constexpr int vrow = 32 * GM * 4;
     static constexpr int sum = qs + ws + bias;
-    static constexpr int bytes = MMA && sum < (HD / 16) * 128 + 768 ? (HD / 16) * 128 + 768 : sum;
+    static constexpr int bytes = sum;
 };
 
-template <int HD, int GM, bool MMA = false>
+template <int HD, int GM>
 __host__ __device__ __forceinline__ size_t partial_smem_bytes(int HG, int mb) {
     const size_t q = (size_t)align_up(HG * GM * HD * 4, 128);
-    const size_t body = (size_t)(MMA ? NSTAGE_M : NSTAGE) * stage_layout(HD, mb, HG, MMA).bytes +
-                        (size_t)NW * WarpArea<HD, GM, MMA>::bytes;
+    const size_t body = (size_t)NSTAGE * stage_layout(HD, mb, HG).bytes + (size_t)NW * WarpArea<HD, GM>::bytes;
     const size_t merge = (size_t)NW * GM * (HD + 2) * 4;
     return q + (body > merge ? body : merge);
 }
@@ -284,10 +267,10 @@ __device__ __forceinline__ void load_wrow(const u64* wt, u64 (&w)[GM]) {
 // ---------------------------------------------------------------------------
 // packed chunk
 // ---------------------------------------------------------------------------
-template <int HD, int GM, bool VPAD = false>
+template <int HD, int GM>
 __device__ __forceinline__ void pbs_issue_stage(const JobDesc& J, int HG, int hg, int t0, int t1, int s,
                                                 unsigned char* stages, const StageLayout& SL, uint64_t* bars,
-                                                int lane, int nslots = NSTAGE) {
+                                                int lane) {
     constexpr int DQ = HDT<HD>::DQ;
     const int ST = stage_tokens(HG);
     const int s0 = t0 + s * ST;
@@ -299,11 +282,10 @@ __device__ __forceinline__ void pbs_issue_stage(const JobDesc& J, int HG, int hg
     // HG*mb >= 16 bytes (plan_attention guarantees one of the two).
     const int mb = J.meta16 ? 2 : 4;
     const int rows = nt / 16, blks = nt / grp;
-    unsigned char* buf = stages + (size_t)(s % nslots) * SL.bytes;
-    uint64_t* bar = &bars[s % nslots];
-    // VPAD: the V words arrive by cp.async (counted as 32 arrivals, not bytes)
-    const uint32_t bytes = (uint32_t)rows * HG * HD * 4 + 2u * blks * HG * HD * mb +
-                           (VPAD ? 0u : (uint32_t)nt * HG * DQ * 4) + 2u * nt * HG * mb + (uint32_t)nt * 8;
+    unsigned char* buf = stages + (size_t)(s % NSTAGE) * SL.bytes;
+    uint64_t* bar = &bars[s % NSTAGE];
+    const uint32_t bytes = (uint32_t)rows * HG * HD * 4 + 2u * blks * HG * HD * mb + (uint32_t)nt * HG * DQ * 4 +
+                           2u * nt * HG * mb + (uint32_t)nt * 8;
     if (lane == 0) mbar_expect_tx(bar, bytes);
     __syncwarp();
     const char* kp = reinterpret_cast<const char*>(J.kp);
@@ -313,25 +295,11 @@ __device__ __forceinline__ void pbs_issue_stage(const JobDesc& J, int HG, int hg
     const char* vs = reinterpret_cast<const char*>(J.vs);
     const char* vz = reinterpret_cast<const char*>(J.vz);
     const char* ids = reinterpret_cast<const char*>(J.ids);
-    if (VPAD) {
-        // tensor-core layout: a token's V words start a row of HG*DQ + 4 words.
-        // Bulk copies this small are issue-bound, so each lane moves its
-        // tokens' rows in 16-byte cp.async pieces (HG*DQ*4 = HG*HD/4 bytes,
-        // a multiple of 16, as is the row stride) and then arrives on the
-        // stage barrier once they have landed.
-        const int rv = (HG * DQ + 4) * 4, cpt = HG * DQ / 4;
-        const char* vsrc = vp + ((size_t)s0 * nkv + h0) * DQ * 4;
-        const size_t tstride = (size_t)nkv * DQ * 4;
-        for (int t = lane; t < nt; t += 32)
-            for (int c = 0; c < cpt; ++c)
-                cp_async16(buf + SL.vw + (size_t)t * rv + c * 16, vsrc + (size_t)t * tstride + c * 16);
-        cp_async_arrive(bar);
-    }
     if (HG == nkv) {
         if (lane == 0) tma_load_1d(buf + SL.kw, kp + (size_t)(s0 / 16) * nkv * HD * 4, rows * HG * HD * 4, bar);
         if (lane == 1) tma_load_1d(buf + SL.ks, ks + (size_t)(s0 / grp) * nkv * HD * mb, blks * HG * HD * mb, bar);
         if (lane == 2) tma_load_1d(buf + SL.kz, kz + (size_t)(s0 / grp) * nkv * HD * mb, blks * HG * HD * mb, bar);
-        if (lane == 3 && !VPAD) tma_load_1d(buf + SL.vw, vp + (size_t)s0 * nkv * DQ * 4, nt * HG * DQ * 4, bar);
+        if (lane == 3) tma_load_1d(buf + SL.vw, vp + (size_t)s0 * nkv * DQ * 4, nt * HG * DQ * 4, bar);
         if (lane == 4) tma_load_1d(buf + SL.vs, vs + (size_t)s0 * nkv * mb, nt * HG * mb, bar);
         if (lane == 5) tma_load_1d(buf + SL.vz, vz + (size_t)s0 * nkv * mb, nt * HG * mb, bar);
         if (lane == 6) tma_load_1d(buf + SL.ids, ids + (size_t)s0 * 8, nt * 8, bar);
@@ -345,9 +313,8 @@ __device__ __forceinline__ void pbs_issue_stage(const JobDesc& J, int HG, int hg
             tma_load_1d(buf + SL.kz + (size_t)i * HG * HD * mb, kz + off, HG * HD * mb, bar);
         }
         for (int i = lane; i < nt; i += 32) {
-            if (!VPAD)
-                tma_load_1d(buf + SL.vw + (size_t)i * HG * DQ * 4, vp + ((size_t)(s0 + i) * nkv + h0) * DQ * 4,
-                            HG * DQ * 4, bar);
+            tma_load_1d(buf + SL.vw + (size_t)i * HG * DQ * 4, vp + ((size_t)(s0 + i) * nkv + h0) * DQ * 4,
+                        HG * DQ * 4, bar);
             const size_t mo = ((size_t)(s0 + i) * nkv + h0) * mb;
             tma_load_1d(buf + SL.vs + (size_t)i * HG * mb, vs + mo, HG * mb, bar);
             tma_load_1d(buf + SL.vz + (size_t)i * HG * mb, vz + mo, HG * mb, bar);
@@ -701,20 +668,31 @@ __device__ __forceinline__ void merge_warps(const JobDesc& J, const float* mbuf,
     }
 }
 
-// MMA: packed chunks run the tensor-core unit (head_dim 64 / 128, GM <= 4,
-// fp16 metadata: the host only selects it then); dense chunks are unchanged.
+// Shared memory of k_attn_partial<HD, GM, MMA>: the SIMT kernel's plan
+// (partial_smem_bytes), or for the tensor-core kernel the query rows followed
+// by one MmaWarpArea per warp (dense chunks use the same warp areas).
+template <int HD, int GM, bool MMA>
+__host__ __device__ __forceinline__ size_t kernel_smem_bytes(int HG, int mb) {
+    if (!MMA) return partial_smem_bytes<HD, GM>(HG, mb);
+    static_assert(!MMA || WarpArea<HD, GM, true>::sum <= MmaWarpArea<HD>::bytes, "dense tables fit a warp area");
+    const size_t q = (size_t)align_up(HG * GM * HD * 4, 128);
+    const size_t body = (size_t)NW * MmaWarpArea<HD>::bytes;
+    const size_t merge = (size_t)NW * GM * (HD + 2) * 4;
+    return q + (body > merge ? body : merge);
+}
+
+// MMA: packed chunks run the tensor-core unit (head_dim 64 / 128, GM <= 4, an
+// even number of kv heads, fp16 metadata: the host only selects it then);
+// dense chunks are unchanged.
 template <int HD, int GM, bool MMA>
 __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __grid_constant__ AttnLaunch L) {
     constexpr int CPL = HDT<HD>::CPL;
-    constexpr int NS = MMA ? NSTAGE_M : NSTAGE;  // stage slots of packed chunks
+    constexpr int NS = NSTAGE;  // stage slots of SIMT packed chunks
     using WA = WarpArea<HD, GM, MMA>;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     __shared__ __align__(8) uint64_t bars[NS];
-    __shared__ int slot_done[NS];  // warps finished with a slot, cumulative over its uses
-    __shared__ int pipe_abort;     // a wait of this CTA timed out
-    __shared__ int pipe_issued;    // stages issued so far
 
     const int job = blockIdx.y / L.nhg;
     const int hg = blockIdx.y - job * L.nhg;
@@ -746,30 +724,25 @@ __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __gr
     const int kvh = hg * HG + kvl;
     const float sc = (1.0f / sqrtf((float)HD)) * kLog2e;  // log2-domain logit scale
     const int mb = J.meta16 ? 2 : 4;
-    const StageLayout SL = stage_layout(HD, mb, HG, MMA);
+    const StageLayout SL = stage_layout(HD, mb, HG);
     const int qbytes = align_up(HG * GM * HD * 4, 128);
     unsigned char* stages = smem + qbytes;
-    unsigned char* wa = stages + (size_t)NS * SL.bytes + (size_t)warp * WA::bytes;
+    unsigned char* wa = MMA ? stages + (size_t)warp * MmaWarpArea<HD>::bytes
+                            : stages + (size_t)NS * SL.bytes + (size_t)warp * WA::bytes;
 
-    // packed chunks: start the first copies before staging Q
+    // SIMT packed chunks: start the first bulk copies before staging Q
     const int ST = stage_tokens(HG);
     const int nst = is_dense ? 0 : ceil_div(t1 - t0, ST);
-    if (!is_dense) {
+    if (!MMA && !is_dense) {
         if (threadIdx.x == 0) {
 #pragma unroll
-            for (int i = 0; i < NS; ++i) {
-                // tensor-core layout: the issuing lane's expect_tx + 32 cp.async arrivals
-                mbar_init(&bars[i], MMA ? 33 : 1);
-                slot_done[i] = 0;
-            }
-            pipe_abort = 0;
-            pipe_issued = min(NS, nst);
+            for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
             mbar_fence_init();
         }
         __syncthreads();
         if (warp == 0)
             for (int s = 0; s < NS && s < nst; ++s)
-                pbs_issue_stage<HD, GM, MMA>(J, HG, hg, t0, t1, s, stages, SL, bars, lane, NS);
+                pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s, stages, SL, bars, lane);
     }
 
     // ---- query rows of this kv-head group: q_s[kvl][g][c] ----
@@ -782,53 +755,40 @@ __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __gr
     __syncthreads();
     const float* qk = q_s + (size_t)kvl * GM * HD;
     const int chunk = blockIdx.x;
-    float* mbuf = reinterpret_cast<float*>(smem + qbytes);  // merge buffer (aliases the stages)
+    float* mbuf = reinterpret_cast<float*>(smem + qbytes);  // merge buffer (aliases the stages / warp areas)
 
     if (MMA && !is_dense) {
         if constexpr (MMA) {
             MmaState<HD> S;
             S.init();
             MmaQ<HD> Qf;
-            if (active) mma_prepare_q<HD, GM>(qk, lane, sc, wa, Qf);
-            // Warps move through the stages independently: each waits for its
-            // stage's copies, runs its unit and releases the slot; the warp that
-            // releases a slot last refills it with the stage NS ahead.  A warp
-            // whose wait times out raises pipe_abort, which ends the other
-            // warps' waits; the CTA then drains its copies in flight and exits.
-            volatile int* abort_v = &pipe_abort;
-            for (int s = 0; s < nst; ++s) {
-                const int slot = s % NS;
-                if (!mbar_wait_abortable(&bars[slot], (uint32_t)((s / NS) & 1), abort_v)) {
-                    *abort_v = 1;
-                    break;
+            // This warp's units: 32-token units r0, r0 + WPH, ... of [t0, t1),
+            // through its own kMmaSlots-deep cp.async pipeline.
+            const int nu_all = ceil_div(t1 - t0, 32);
+            const int nu = active && r0 < nu_all ? ceil_div(nu_all - r0, WPH) : 0;
+            if (nu > 0) {
+                mma_prepare_q<HD, GM>(qk, lane, sc, wa, Qf);
+                auto issue = [&](int k) {
+                    const int s0 = t0 + (r0 + k * WPH) * 32;
+                    mma_issue<HD>(J, kvh, s0, min(32, t1 - s0), wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes,
+                                  lane);
+                };
+#pragma unroll
+                for (int k = 0; k < kMmaSlots - 1; ++k) {
+                    if (k < nu) issue(k);
+                    cp_async_commit();
                 }
-                const unsigned char* buf = stages + (size_t)slot * SL.bytes;
-                const int s0 = t0 + s * ST;
-                const int nt = min(ST, t1 - s0);
-                if (active && r0 * 32 < nt) pbs_unit_mma<HD, GM>(J, HG, G, kvl, kvh, lane, D, buf, SL, s0, nt, r0, Qf, wa, S);
-                __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    __threadfence_block();
-                    last = atomicAdd(&slot_done[slot], 1) == (s / NS + 1) * NW - 1;
-                    if (last) __threadfence_block();
+                for (int k = 0; k < nu; ++k) {
+                    // refill the slot unit k-1 used (released at the end of its iteration)
+                    if (k + kMmaSlots - 1 < nu) issue(k + kMmaSlots - 1);
+                    cp_async_commit();
+                    cp_async_wait<kMmaSlots - 1>();  // unit k's copies (this lane's) have landed
+                    __syncwarp();                    // ... and every lane's are visible
+                    const int s0 = t0 + (r0 + k * WPH) * 32;
+                    pbs_unit_mma<HD, GM>(J, G, kvh, lane, D, wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes,
+                                         s0, min(32, t1 - s0), Qf, wa, S);
                 }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last && s + NS < nst && *abort_v == 0) {
-                    pbs_issue_stage<HD, GM, MMA>(J, HG, hg, t0, t1, s + NS, stages, SL, bars, lane, NS);
-                    if (lane == 0) atomicMax(&pipe_issued, s + NS + 1);
-                }
-            }
-            __syncthreads();
-            if (pipe_abort) {
-                if (threadIdx.x == 0) {
-                    // the last stage issued into each slot; earlier ones were consumed
-                    for (int k = max(0, pipe_issued - NS); k < pipe_issued; ++k)
-                        (void)mbar_wait_bounded(&bars[k % NS], (uint32_t)((k / NS) & 1));
-                    atomicCAS(&g_device_error, 0, (int)TT_ERR_TIMEOUT);
-                    if (J.ctr) atomicCAS(const_cast<int*>(&J.ctr->error), 0, (int)TT_ERR_TIMEOUT);
-                }
-                return;
+                cp_async_wait<0>();
             }
             float m, l, o[HD / 16][2];
             mma_finish<HD>(S, m, l, o);

@@ -1,7 +1,8 @@
 // tt_pbs_mma.cuh -- packed-tier (2-bit) attention on the tensor cores with
 // mma.sync.m16n8k16 (f16 operands, f32 accumulation).  Included by
 // tt_partial.cuh.  Used for head_dim 64 / 128, at most 4 query heads per kv
-// head and fp16 metadata; the SIMT unit covers the other shapes.
+// head, an even number of kv heads and fp16 metadata; the SIMT unit covers the
+// other shapes.
 //
 // Fragment layout of m16n8k16 (row.col); lane = 4*gid + tig:
 //   A a0:(row gid, k-slots 2tig,2tig+1) a1:(gid+8, same) a2:(gid, 2tig+8,+9) a3:(gid+8, same)
@@ -22,8 +23,8 @@
 //       in the mantissa of f16 4.0.
 //   B = q' * s split into hi/lo with f16 FMAs: h = q'h*s, r = q'h*s - h (exact),
 //       lo = q'l*s + r; q' = q * 2^-e_g with |q'| < 1, so |q' s| <= 65504.
-//   bias = -4 sum_c q' s + sum_c q' z: one MMA per k-step with the scale and
-//       zero rows of both blocks as A rows 0..3 and the q' fragments as B.
+//   bias = -4 sum_c q' s + sum_c q' z: one MMA per k-step with the scale rows
+//       (A rows 0..7) and zero rows (8..15) of both blocks and the q' fragments as B.
 // PV per 32-token unit, out[c][g] = sum_t (p_t vs_t) (4 + code_tc):
 //   A = 4 + code from the V words (16 channels of one token), same gather;
 //   B = p*vs*2^-E split hi/lo; E is kept while a unit's largest weight stays
@@ -31,22 +32,42 @@
 //   tile result (hi + lo columns) is folded into the running f32 output as
 //   acc = acc * alpha * 2^(E_old - E_new) + tile.
 // In both D layouts a thread holds query head g = tig.
+//
+// Staging: each warp runs its own two-slot pipeline over its units.  Its part
+// of a unit (K words, block scales/zeros, V words, V scale/zero, ids: 3.5 KB
+// at head_dim 128) moves with per-lane 16-byte cp.async (4-byte for the V
+// scale/zero pairs) into a warp-private slot, waited for with
+// cp.async.wait_group + __syncwarp.  No warp waits for another, and no copy is
+// small enough to be issue-bound.
 #pragma once
 
 namespace tt {
 
-constexpr int kMmaWRow = 48;  // halves per row of the PV weight table (32 tokens + pad)
+constexpr int kMmaWRow = 48;   // halves per row of the PV weight table (32 tokens + pad)
+constexpr int kMmaSlots = 2;   // stages in flight per warp
 
+// One warp's stage: its kv head's part of one 32-token unit.
 template <int HD>
-struct MmaWarpArea {
-    static constexpr int wtab = 8 * kMmaWRow * 2;  // [n][position] f16
-    static constexpr int qtab = (HD / 16) * 32 * 4; // [ks][head*4 + tig][2] f16x2: q' hi
-    static constexpr int bytes = wtab + qtab;
+struct MmaStage {
+    static constexpr int kw = 0;                   // [2 rows of 16 tokens][HD] K words
+    static constexpr int ks = kw + 2 * HD * 4;     // [2 blocks][HD] f16 K scales (1 block used with group 32)
+    static constexpr int kz = ks + 2 * HD * 2;     // [2 blocks][HD] f16 K zeros
+    static constexpr int vw = kz + 2 * HD * 2;     // [32 tokens][HD/16] V words
+    static constexpr int vs = vw + 32 * HD / 4;    // [32 tokens][2] f16 V scales of heads (h & ~1, h | 1)
+    static constexpr int vz = vs + 32 * 4;         // same for the V zeros
+    static constexpr int ids = vz + 32 * 4;        // [32] token ids
+    static constexpr int bytes = (ids + 32 * 8 + 127) / 128 * 128;
 };
 
-// V words of one staged token occupy HG*DQ + 4 words (the pad spreads the four
-// tokens a load instruction touches over distinct banks).
-__host__ __device__ __forceinline__ int mma_vrow_words(int HG, int HD) { return HG * (HD / 16) + 4; }
+// Per-warp shared memory of the tensor-core unit: its stage slots, the PV
+// weight table and the q' hi table.
+template <int HD>
+struct MmaWarpArea {
+    static constexpr int slots = kMmaSlots * MmaStage<HD>::bytes;
+    static constexpr int wtab = slots;                  // [n][position] f16
+    static constexpr int qtab = wtab + 8 * kMmaWRow * 2; // [ks][head*4 + tig | 16 + tig][2] f16x2: q' hi | zero
+    static constexpr int bytes = (qtab + (HD / 16) * 40 * 4 + 127) / 128 * 128;
+};
 
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                               uint32_t b0, uint32_t b1) {
@@ -71,31 +92,45 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<ui
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }  // |e| <= 126
 
+// cp.async of 4 bytes (L1-allocating form; the 16-byte form is cp_async16)
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Two A registers (rows gid, gid+8) for the k-slot pair whose words are w0, w1:
-// sel gathers byte gid/4 and 2+gid/4 of both words, sft = 2*(gid%4).
-__device__ __forceinline__ void a_pair(uint32_t w0, uint32_t w1, uint32_t sel, int sft, uint32_t& lo_row,
-                                       uint32_t& hi_row) {
+// sel gathers byte gid/4 and 2+gid/4 of both words, sft = 2*(gid%4) and
+// m8 = 2^(8 - sft) (the left shift runs as an integer multiply, on the FMA
+// pipe, next to the ALU pipe's PRMT / shift / LOP3).
+__device__ __forceinline__ void a_pair(uint32_t w0, uint32_t w1, uint32_t sel, uint32_t sft, uint32_t m8,
+                                       uint32_t& lo_row, uint32_t& hi_row) {
     const uint32_t P = __byte_perm(w0, w1, sel);
-    lo_row = ((P << (8 - sft)) & 0x03000300u) | 0x44004400u;
+    lo_row = ((P * m8) & 0x03000300u) | 0x44004400u;
     hi_row = ((P >> sft) & 0x03000300u) | 0x44004400u;
 }
 
-// B register (n = gid) of q'*s for two channels: hi lanes h, lo lanes q'l*s + (q'h*s - h).
-__device__ __forceinline__ uint32_t b_qs(uint32_t qh, uint32_t qx, uint32_t s, uint32_t lomask) {
-    const __half2 sv = u2h(s), qhv = u2h(qh);
-    const __half2 h = __hmul2(qhv, sv);
-    const uint32_t r = h2u(__hfma2(qhv, sv, __hneg2(h))) & lomask;
-    return h2u(__hfma2(u2h(qx), sv, u2h(r)));
+// B register (n = gid) of q'*s for two channels.  qm is q' hi on lo (odd)
+// lanes and zero on hi (even) lanes, qx the lane's own part of q': hi lanes
+// get round(q'h*s), lo lanes q'l*s + (q'h*s - round(q'h*s)), the residual
+// being exact in f16.
+__device__ __forceinline__ uint32_t b_qs(uint32_t qm, uint32_t qx, uint32_t s) {
+    const __half2 sv = u2h(s), qmv = u2h(qm);
+    const __half2 h = __hmul2(qmv, sv);
+    const __half2 r = __hfma2(qmv, sv, __hneg2(h));
+    return h2u(__hfma2(u2h(qx), sv, r));
 }
 
-// Per-thread q' fragments for n = gid (head gid/2, part gid&1) and the
-// power-of-two scale of head tig.  The hi part, which both lanes of a head
-// need, sits in the warp's q table (qtab of MmaWarpArea).
+// Per-thread B fragments of q' for n = gid (head gid/2, part gid&1) and the
+// power-of-two scale of head tig.  The hi part, which the lo lanes also need,
+// goes to the warp's q table (with zero rows that the hi lanes read).
 template <int HD>
 struct MmaQ {
     static constexpr int KS = HD / 16;
     uint32_t qx[KS][2];  // the B fragment of q' itself: hi (even gid) or lo (odd gid)
-    uint32_t lomask;     // all ones on odd gid
     float up_sc;         // 2^e of head tig times the log2-domain logit scale
 };
 
@@ -120,16 +155,15 @@ __device__ __forceinline__ void mma_prepare_q(const float* qk, int lane, float s
     e = max(-100, min(100, e));
     const float down = pow2f(-e);
     const bool odd = (gid & 1) != 0;
-    Q.lomask = odd ? 0xffffffffu : 0u;
+    uint32_t* qtab = reinterpret_cast<uint32_t*>(wa + MmaWarpArea<HD>::qtab);
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
         const float x0 = v[ks].x * down, x1 = v[ks].y * down, x2 = v[ks].z * down, x3 = v[ks].w * down;
         const __half2 h01 = __floats2half2_rn(x0, x1), h23 = __floats2half2_rn(x2, x3);
         const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
         const __half2 l01 = __floats2half2_rn(x0 - f01.x, x1 - f01.y), l23 = __floats2half2_rn(x2 - f23.x, x3 - f23.y);
-        if (!odd)
-            *reinterpret_cast<uint2*>(wa + MmaWarpArea<HD>::wtab + (size_t)(ks * 32 + (g * 4 + tig) * 2) * 4) =
-                make_uint2(h2u(h01), h2u(h23));
+        if (!odd) *reinterpret_cast<uint2*>(qtab + ks * 40 + (g * 4 + tig) * 2) = make_uint2(h2u(h01), h2u(h23));
+        if (gid == 0) *reinterpret_cast<uint2*>(qtab + ks * 40 + (16 + tig) * 2) = make_uint2(0u, 0u);
         Q.qx[ks][0] = odd ? h2u(l01) : h2u(h01);
         Q.qx[ks][1] = odd ? h2u(l23) : h2u(h23);
     }
@@ -152,6 +186,47 @@ struct MmaState {
     }
 };
 
+// Copies the warp's part of the unit [s0, s0 + nt) (nt = 16 or 32) for kv head
+// kvh into stage st with per-lane cp.async; the caller commits the group.
+// Every source offset is a multiple of 16 bytes (4 for the V scale/zero pairs:
+// the number of kv heads is even), every size a multiple of the copy size.
+template <int HD>
+__device__ __forceinline__ void mma_issue(const JobDesc& J, int kvh, int s0, int nt, unsigned char* st, int lane) {
+    using SL = MmaStage<HD>;
+    constexpr int DQ = HD / 16;
+    const int nkv = J.nkv;
+    const int gsh = J.grp == 32 ? 5 : 4;
+    const char* kp = reinterpret_cast<const char*>(J.kp);
+    const char* ksp = reinterpret_cast<const char*>(J.ks);
+    const char* kzp = reinterpret_cast<const char*>(J.kz);
+    const char* vp = reinterpret_cast<const char*>(J.vp);
+    const char* vsp = reinterpret_cast<const char*>(J.vs);
+    const char* vzp = reinterpret_cast<const char*>(J.vz);
+    const char* idp = reinterpret_cast<const char*>(J.ids);
+    const int rows = nt >> 4;
+    for (int i = lane; i < rows * (HD / 4); i += 32) {  // K words: HD/4 chunks per 16-token row
+        const int r = i / (HD / 4), c = i - r * (HD / 4);
+        cp_async16(st + SL::kw + r * HD * 4 + c * 16, kp + ((size_t)((s0 >> 4) + r) * nkv + kvh) * HD * 4 + c * 16);
+    }
+    const int nb = max(1, nt >> gsh);
+    for (int i = lane; i < nb * (HD / 8); i += 32) {  // K scale / zero: HD/8 chunks per block
+        const int b = i / (HD / 8), c = i - b * (HD / 8);
+        const size_t off = ((size_t)((s0 >> gsh) + b) * nkv + kvh) * HD * 2 + c * 16;
+        cp_async16(st + SL::ks + b * HD * 2 + c * 16, ksp + off);
+        cp_async16(st + SL::kz + b * HD * 2 + c * 16, kzp + off);
+    }
+    for (int i = lane; i < nt * (HD / 64); i += 32) {  // V words: HD/64 chunks per token
+        const int t = i / (HD / 64), c = i - t * (HD / 64);
+        cp_async16(st + SL::vw + t * DQ * 4 + c * 16, vp + ((size_t)(s0 + t) * nkv + kvh) * DQ * 4 + c * 16);
+    }
+    for (int t = lane; t < nt; t += 32) {  // V scale / zero of heads (kvh & ~1, kvh | 1)
+        const size_t off = ((size_t)(s0 + t) * nkv + (kvh & ~1)) * 2;
+        cp_async4(st + SL::vs + t * 4, vsp + off);
+        cp_async4(st + SL::vz + t * 4, vzp + off);
+    }
+    if (lane < nt / 2) cp_async16(st + SL::ids + lane * 16, idp + (size_t)s0 * 8 + lane * 16);
+}
+
 // position of unit-local token t in the PV weight table (k-slot order)
 __device__ __forceinline__ int mma_wpos(int t) { return (t & 16) + 4 * (t & 3) + ((t & 15) >> 2); }
 
@@ -161,88 +236,89 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x (PTX ex2.approx; 
     return y;
 }
 
+// One 32-token unit [s0, s0 + nt) of kv head kvh from stage st.
 template <int HD, int GM>
-__device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, int kvl, int kvh, int lane, int D,
-                                             const unsigned char* buf, const StageLayout& SL, int s0, int nt, int r,
-                                             const MmaQ<HD>& Q, unsigned char* wa, MmaState<HD>& S) {
+__device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, int lane, int D,
+                                             const unsigned char* st, int s0, int nt, const MmaQ<HD>& Q,
+                                             unsigned char* wa, MmaState<HD>& S) {
     static_assert((HD == 64 || HD == 128) && GM <= 4, "tensor-core unit shape");
-    static_assert(MmaWarpArea<HD>::bytes <= WarpArea<HD, GM, true>::bytes, "weight table fits the warp area");
+    using SL = MmaStage<HD>;
     constexpr int KS = HD / 16, DQ = HD / 16;
     const int gid = lane >> 2, tig = lane & 3;
-    const int sft = 2 * (gid & 3);
+    const uint32_t sft = 2 * (gid & 3);
+    const uint32_t m8 = 1u << (8 - sft);
     const uint32_t sel = 0x6420u + 0x1111u * (uint32_t)(gid >> 2);
-    __half* wtab = reinterpret_cast<__half*>(wa);
+    __half* wtab = reinterpret_cast<__half*>(wa + MmaWarpArea<HD>::wtab);
     const int gsh = J.grp == 32 ? 5 : 4;  // log2 of the block size (16 or 32)
-    const int ub = r * 32;  // unit start within the stage
-    const uint32_t* kw_s = reinterpret_cast<const uint32_t*>(buf + SL.kw);
-    const __half* ks_s = reinterpret_cast<const __half*>(buf + SL.ks);
-    const __half* kz_s = reinterpret_cast<const __half*>(buf + SL.kz);
-    const uint32_t* vw_s = reinterpret_cast<const uint32_t*>(buf + SL.vw);
-    const __half* vs_s = reinterpret_cast<const __half*>(buf + SL.vs);
-    const __half* vz_s = reinterpret_cast<const __half*>(buf + SL.vz);
-    const int64_t* ids_s = reinterpret_cast<const int64_t*>(buf + SL.ids);
-    // Second half-unit present?  (nt is a multiple of 16.)  When it is not,
-    // its rows still run through the MMAs on whatever the stage buffer holds
-    // (in bounds: ub + 32 <= ST); every value derived from them is masked.
-    const bool two = ub + 16 < nt;
+    const uint32_t* kw_s = reinterpret_cast<const uint32_t*>(st + SL::kw);
+    const __half* ks_s = reinterpret_cast<const __half*>(st + SL::ks);
+    const __half* kz_s = reinterpret_cast<const __half*>(st + SL::kz);
+    const uint32_t* vw_s = reinterpret_cast<const uint32_t*>(st + SL::vw);
+    const __half* vs_s = reinterpret_cast<const __half*>(st + SL::vs) + (kvh & 1);
+    const __half* vz_s = reinterpret_cast<const __half*>(st + SL::vz) + (kvh & 1);
+    const int64_t* ids_s = reinterpret_cast<const int64_t*>(st + SL::ids);
+    // Second half-unit present?  (nt is 16 or 32.)  When it is not, its rows
+    // still run through the MMAs on whatever the slot holds (in bounds); every
+    // value derived from them is masked.
+    const bool two = nt > 16;
 
     // ---- bias rows and QK, three independent accumulation chains ----
-    // bias A rows 0..3: scale / zero of the block of half 0 / half 1
+    // bias A rows: row gid = scale, row gid+8 = zero of the block of half gid&1
+    // (lanes 0..7 carry the two halves; the other rows repeat them, unused)
     float bd[4] = {0.f, 0.f, 0.f, 0.f};
     float dq[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     {
-        const bool rowv = gid < 4;
-        const __half* mrow =
-            ((gid & 1) ? kz_s : ks_s) + ((size_t)((ub + 16 * ((gid >> 1) & 1)) >> gsh) * HG + kvl) * HD + 4 * tig;
-        const uint32_t* kw0 = kw_s + ((size_t)(ub >> 4) * HG + kvl) * HD + 4 * tig;
-        const uint32_t* kw1 = kw0 + (size_t)HG * HD;
-        const __half* sb0 = ks_s + ((size_t)(ub >> gsh) * HG + kvl) * HD + 4 * tig;
-        const __half* sb1 = ks_s + ((size_t)((ub + 16) >> gsh) * HG + kvl) * HD + 4 * tig;
+        const int mo = ((16 * (gid & 1)) >> gsh) * HD + 4 * tig;
+        const uint32_t* ms_row = reinterpret_cast<const uint32_t*>(ks_s + mo);
+        const uint32_t* mz_row = reinterpret_cast<const uint32_t*>(kz_s + mo);
+        const uint32_t* kw0 = kw_s + 4 * tig;
+        const uint32_t* kw1 = kw0 + HD;
+        const __half* sb0 = ks_s + 4 * tig;
+        const __half* sb1 = ks_s + (16 >> gsh) * HD + 4 * tig;
         const bool shared_blk = gsh == 5;  // both halves in one block: same B fragments
-        const uint32_t* qh_t = reinterpret_cast<const uint32_t*>(wa + MmaWarpArea<HD>::wtab) + ((gid >> 1) * 4 + tig) * 2;
+        const uint32_t* qm_t = reinterpret_cast<const uint32_t*>(wa + MmaWarpArea<HD>::qtab) +
+                               ((gid & 1) ? (gid >> 1) * 4 + tig : 16 + tig) * 2;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-            uint2 m2 = make_uint2(0u, 0u);
-            if (rowv) m2 = *reinterpret_cast<const uint2*>(mrow + 16 * ks);
-            mma_f16_16816(bd, m2.x, 0u, m2.y, 0u, Q.qx[ks][0], Q.qx[ks][1]);
+            mma_f16_16816(bd, ms_row[8 * ks], mz_row[8 * ks], ms_row[8 * ks + 1], mz_row[8 * ks + 1], Q.qx[ks][0],
+                          Q.qx[ks][1]);
             const uint4 w0 = *reinterpret_cast<const uint4*>(kw0 + 16 * ks);
             const uint4 w1 = *reinterpret_cast<const uint4*>(kw1 + 16 * ks);
             const uint2 sv0 = *reinterpret_cast<const uint2*>(sb0 + 16 * ks);
-            const uint2 qh = *reinterpret_cast<const uint2*>(qh_t + ks * 32);
-            const uint32_t b00 = b_qs(qh.x, Q.qx[ks][0], sv0.x, Q.lomask);
-            const uint32_t b01 = b_qs(qh.y, Q.qx[ks][1], sv0.y, Q.lomask);
+            const uint2 qm = *reinterpret_cast<const uint2*>(qm_t + ks * 40);
+            const uint32_t b00 = b_qs(qm.x, Q.qx[ks][0], sv0.x);
+            const uint32_t b01 = b_qs(qm.y, Q.qx[ks][1], sv0.y);
             uint32_t b10 = b00, b11 = b01;
             if (!shared_blk) {
                 const uint2 sv1 = *reinterpret_cast<const uint2*>(sb1 + 16 * ks);
-                b10 = b_qs(qh.x, Q.qx[ks][0], sv1.x, Q.lomask);
-                b11 = b_qs(qh.y, Q.qx[ks][1], sv1.y, Q.lomask);
+                b10 = b_qs(qm.x, Q.qx[ks][0], sv1.x);
+                b11 = b_qs(qm.y, Q.qx[ks][1], sv1.y);
             }
             uint32_t a0, a1, a2, a3;
-            a_pair(w0.x, w0.y, sel, sft, a0, a1);
-            a_pair(w0.z, w0.w, sel, sft, a2, a3);
+            a_pair(w0.x, w0.y, sel, sft, m8, a0, a1);
+            a_pair(w0.z, w0.w, sel, sft, m8, a2, a3);
             mma_f16_16816(dq[0], a0, a1, a2, a3, b00, b01);
-            a_pair(w1.x, w1.y, sel, sft, a0, a1);
-            a_pair(w1.z, w1.w, sel, sft, a2, a3);
+            a_pair(w1.x, w1.y, sel, sft, m8, a0, a1);
+            a_pair(w1.z, w1.w, sel, sft, m8, a2, a3);
             mma_f16_16816(dq[1], a0, a1, a2, a3, b10, b11);
         }
     }
-    const float beta = bd[0] + bd[1];  // row gid, head tig
+    // this lane's half (gid&1), head tig: sum q'z - 4 sum q's
+    const float bias_own = (bd[2] + bd[3]) - 4.0f * (bd[0] + bd[1]);
     float s[4];  // unit-local tokens gid, gid+8, 16+gid, 24+gid; head tig
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
-        const float bsum = __shfl_sync(0xffffffffu, beta, 8 * hf + tig);
-        const float bzer = __shfl_sync(0xffffffffu, beta, 8 * hf + 4 + tig);
-        const float bias = bzer - 4.0f * bsum;
+        const float bias = __shfl_sync(0xffffffffu, bias_own, 4 * hf + tig);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            const int t = ub + 16 * hf + gid + 8 * j;  // stage-local token
+            const int t = 16 * hf + gid + 8 * j;
             const bool live = (hf == 0 || two) && tig < G && ids_s[t] != -1;
             s[2 * hf + j] = live ? ((dq[hf][2 * j] + dq[hf][2 * j + 1]) + bias) * Q.up_sc : -INFINITY;
         }
     }
     // ---- logits to scratch ----
     if (tig < G) {
-        float* srow = J.scores + (size_t)(kvh * G + tig) * J.score_stride + D + s0 + ub;
+        float* srow = J.scores + (size_t)(kvh * G + tig) * J.score_stride + D + s0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int t = 16 * (k >> 1) + gid + 8 * (k & 1);
@@ -271,11 +347,11 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, in
     float wmx = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int t = ub + 16 * (k >> 1) + gid + 8 * (k & 1);
+        const int t = 16 * (k >> 1) + gid + 8 * (k & 1);
         float vsc = 0.f, vzr = 0.f;
         if (k < 2 || two) {
-            vsc = __half2float(vs_s[(size_t)t * HG + kvl]);
-            vzr = __half2float(vz_s[(size_t)t * HG + kvl]);
+            vsc = __half2float(vs_s[2 * t]);
+            vzr = __half2float(vz_s[2 * t]);
         }
         ws[k] = p[k] * vsc;
         S.sws += ws[k];
@@ -302,10 +378,9 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, in
     }
     __syncwarp();
     // ---- PV: channel tiles of 16, two k-steps of 16 tokens each ----
-    const int RV = mma_vrow_words(HG, HD);
     const uint2 bw0 = *reinterpret_cast<const uint2*>(wtab + gid * kMmaWRow + 4 * tig);
     const uint2 bw1 = *reinterpret_cast<const uint2*>(wtab + gid * kMmaWRow + 16 + 4 * tig);
-    const uint32_t* vrow = vw_s + (size_t)(ub + tig) * RV + kvl * DQ;
+    const uint32_t* vrow = vw_s + tig * DQ;
 #pragma unroll
     for (int mh = 0; mh < DQ / 4; ++mh) {
         float d[4][4];  // channel tiles 4mh..4mh+3
@@ -313,8 +388,7 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, in
         for (int kk = 0; kk < 2; ++kk) {
             uint4 vv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                vv[i] = *reinterpret_cast<const uint4*>(vrow + (size_t)(16 * kk + 4 * i) * RV + 4 * mh);
+            for (int i = 0; i < 4; ++i) vv[i] = *reinterpret_cast<const uint4*>(vrow + (16 * kk + 4 * i) * DQ + 4 * mh);
             const uint2 bw = kk == 0 ? bw0 : bw1;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -323,8 +397,8 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int HG, int G, in
                 const uint32_t w2 = q == 0 ? vv[2].x : q == 1 ? vv[2].y : q == 2 ? vv[2].z : vv[2].w;
                 const uint32_t w3 = q == 0 ? vv[3].x : q == 1 ? vv[3].y : q == 2 ? vv[3].z : vv[3].w;
                 uint32_t a0, a1, a2, a3;
-                a_pair(w0, w1, sel, sft, a0, a1);
-                a_pair(w2, w3, sel, sft, a2, a3);
+                a_pair(w0, w1, sel, sft, m8, a0, a1);
+                a_pair(w2, w3, sel, sft, m8, a2, a3);
                 if (kk == 0) mma_f16_16816_z(d[q], a0, a1, a2, a3, bw.x, bw.y);
                 else mma_f16_16816(d[q], a0, a1, a2, a3, bw.x, bw.y);
             }
