@@ -78,16 +78,6 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// D = A*B (zero accumulator)
-__device__ __forceinline__ void mma_f16_16816_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                                uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
-}
-
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }  // |e| <= 126
@@ -102,15 +92,39 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Two A registers (rows gid, gid+8) for the k-slot pair whose words are w0, w1:
-// sel gathers byte gid/4 and 2+gid/4 of both words, sft = 2*(gid%4) and
-// m8 = 2^(8 - sft) (the left shift runs as an integer multiply, on the FMA
-// pipe, next to the ALU pipe's PRMT / shift / LOP3).
-__device__ __forceinline__ void a_pair(uint32_t w0, uint32_t w1, uint32_t sel, uint32_t sft, uint32_t m8,
-                                       uint32_t& lo_row, uint32_t& hi_row) {
-    const uint32_t P = __byte_perm(w0, w1, sel);
-    lo_row = ((P * m8) & 0x03000300u) | 0x44004400u;
-    hi_row = ((P >> sft) & 0x03000300u) | 0x44004400u;
+// d += A*B (ZERO_C: d = A*B) where A is the 4+code fragment of the k-slot
+// pairs (w0, w1) and (w2, w3) for rows gid and gid+8: sel gathers byte gid/4
+// and 2+gid/4 of both words (PRMT), the fields move to mantissa bits 8-9 of
+// each f16 half by a multiply with m8 = 2^(8 - sft) (row gid, on the FMA pipe)
+// or a right shift by sft = 2*(gid%4) (row gid+8), and LOP3 masks them and
+// sets the exponent of 4.0.  One PTX block, so the LOP3 results are the MMA's
+// operand registers.
+template <bool ZERO_C>
+__device__ __forceinline__ void mma_codes(float (&d)[4], uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                          uint32_t sel, uint32_t sft, uint32_t m8, uint32_t b0, uint32_t b1) {
+    if constexpr (ZERO_C) {
+        asm volatile(
+            "{\n .reg .b32 p0, p1, t0, t1, t2, t3, a0, a1, a2, a3;\n"
+            " prmt.b32 p0, %4, %5, %8;\n prmt.b32 p1, %6, %7, %8;\n"
+            " mul.lo.u32 t0, p0, %10;\n shr.b32 t1, p0, %9;\n mul.lo.u32 t2, p1, %10;\n shr.b32 t3, p1, %9;\n"
+            " lop3.b32 a0, t0, 0x03000300, 0x44004400, 0xea;\n lop3.b32 a1, t1, 0x03000300, 0x44004400, 0xea;\n"
+            " lop3.b32 a2, t2, 0x03000300, 0x44004400, 0xea;\n lop3.b32 a3, t3, 0x03000300, 0x44004400, 0xea;\n"
+            " mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {a0,a1,a2,a3}, {%11,%12}, "
+            "{%13,%13,%13,%13};\n}\n"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(w0), "r"(w1), "r"(w2), "r"(w3), "r"(sel), "r"(sft), "r"(m8), "r"(b0), "r"(b1), "f"(0.f));
+    } else {
+        asm volatile(
+            "{\n .reg .b32 p0, p1, t0, t1, t2, t3, a0, a1, a2, a3;\n"
+            " prmt.b32 p0, %4, %5, %8;\n prmt.b32 p1, %6, %7, %8;\n"
+            " mul.lo.u32 t0, p0, %10;\n shr.b32 t1, p0, %9;\n mul.lo.u32 t2, p1, %10;\n shr.b32 t3, p1, %9;\n"
+            " lop3.b32 a0, t0, 0x03000300, 0x44004400, 0xea;\n lop3.b32 a1, t1, 0x03000300, 0x44004400, 0xea;\n"
+            " lop3.b32 a2, t2, 0x03000300, 0x44004400, 0xea;\n lop3.b32 a3, t3, 0x03000300, 0x44004400, 0xea;\n"
+            " mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {a0,a1,a2,a3}, {%11,%12}, "
+            "{%0,%1,%2,%3};\n}\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(w0), "r"(w1), "r"(w2), "r"(w3), "r"(sel), "r"(sft), "r"(m8), "r"(b0), "r"(b1));
+    }
 }
 
 // B register (n = gid) of q'*s for two channels.  qm is q' hi on lo (odd)
@@ -196,35 +210,39 @@ __device__ __forceinline__ void mma_issue(const JobDesc& J, int kvh, int s0, int
     constexpr int DQ = HD / 16;
     const int nkv = J.nkv;
     const int gsh = J.grp == 32 ? 5 : 4;
-    const char* kp = reinterpret_cast<const char*>(J.kp);
-    const char* ksp = reinterpret_cast<const char*>(J.ks);
-    const char* kzp = reinterpret_cast<const char*>(J.kz);
-    const char* vp = reinterpret_cast<const char*>(J.vp);
-    const char* vsp = reinterpret_cast<const char*>(J.vs);
-    const char* vzp = reinterpret_cast<const char*>(J.vz);
-    const char* idp = reinterpret_cast<const char*>(J.ids);
+    // per-array bases of this unit (uniform across the warp) + 32-bit lane offsets
+    const char* kb = reinterpret_cast<const char*>(J.kp) + ((size_t)(s0 >> 4) * nkv + kvh) * (HD * 4);
+    const size_t moff = ((size_t)(s0 >> gsh) * nkv + kvh) * (HD * 2);
+    const char* sb = reinterpret_cast<const char*>(J.ks) + moff;
+    const char* zb = reinterpret_cast<const char*>(J.kz) + moff;
+    const char* vb = reinterpret_cast<const char*>(J.vp) + ((size_t)s0 * nkv + kvh) * (DQ * 4);
+    const size_t soff = ((size_t)s0 * nkv + (kvh & ~1)) * 2;
+    const char* vsb = reinterpret_cast<const char*>(J.vs) + soff;
+    const char* vzb = reinterpret_cast<const char*>(J.vz) + soff;
+    const char* ib = reinterpret_cast<const char*>(J.ids) + (size_t)s0 * 8;
     const int rows = nt >> 4;
-    for (int i = lane; i < rows * (HD / 4); i += 32) {  // K words: HD/4 chunks per 16-token row
-        const int r = i / (HD / 4), c = i - r * (HD / 4);
-        cp_async16(st + SL::kw + r * HD * 4 + c * 16, kp + ((size_t)((s0 >> 4) + r) * nkv + kvh) * HD * 4 + c * 16);
+    const int krow = nkv * HD * 4;            // bytes between K word rows (16 tokens)
+    for (int i = lane; i < rows * (HD / 4); i += 32) {  // K words: HD/4 chunks per row
+        const int r = i / (HD / 4), c = i % (HD / 4);
+        cp_async16(st + SL::kw + r * HD * 4 + c * 16, kb + r * krow + c * 16);
     }
     const int nb = max(1, nt >> gsh);
+    const int mblk = nkv * HD * 2;            // bytes between metadata blocks
     for (int i = lane; i < nb * (HD / 8); i += 32) {  // K scale / zero: HD/8 chunks per block
-        const int b = i / (HD / 8), c = i - b * (HD / 8);
-        const size_t off = ((size_t)((s0 >> gsh) + b) * nkv + kvh) * HD * 2 + c * 16;
-        cp_async16(st + SL::ks + b * HD * 2 + c * 16, ksp + off);
-        cp_async16(st + SL::kz + b * HD * 2 + c * 16, kzp + off);
+        const int b = i / (HD / 8), c = i % (HD / 8);
+        cp_async16(st + SL::ks + b * HD * 2 + c * 16, sb + b * mblk + c * 16);
+        cp_async16(st + SL::kz + b * HD * 2 + c * 16, zb + b * mblk + c * 16);
     }
+    const int vtok = nkv * DQ * 4;            // bytes between tokens' V words
     for (int i = lane; i < nt * (HD / 64); i += 32) {  // V words: HD/64 chunks per token
-        const int t = i / (HD / 64), c = i - t * (HD / 64);
-        cp_async16(st + SL::vw + t * DQ * 4 + c * 16, vp + ((size_t)(s0 + t) * nkv + kvh) * DQ * 4 + c * 16);
+        const int t = i / (HD / 64), c = i % (HD / 64);
+        cp_async16(st + SL::vw + t * DQ * 4 + c * 16, vb + t * vtok + c * 16);
     }
-    for (int t = lane; t < nt; t += 32) {  // V scale / zero of heads (kvh & ~1, kvh | 1)
-        const size_t off = ((size_t)(s0 + t) * nkv + (kvh & ~1)) * 2;
-        cp_async4(st + SL::vs + t * 4, vsp + off);
-        cp_async4(st + SL::vz + t * 4, vzp + off);
+    if (lane < nt) {  // V scale / zero of heads (kvh & ~1, kvh | 1)
+        cp_async4(st + SL::vs + lane * 4, vsb + lane * nkv * 2);
+        cp_async4(st + SL::vz + lane * 4, vzb + lane * nkv * 2);
     }
-    if (lane < nt / 2) cp_async16(st + SL::ids + lane * 16, idp + (size_t)s0 * 8 + lane * 16);
+    if (lane < nt / 2) cp_async16(st + SL::ids + lane * 16, ib + lane * 16);
 }
 
 // position of unit-local token t in the PV weight table (k-slot order)
@@ -294,13 +312,8 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, i
                 b10 = b_qs(qm.x, Q.qx[ks][0], sv1.x);
                 b11 = b_qs(qm.y, Q.qx[ks][1], sv1.y);
             }
-            uint32_t a0, a1, a2, a3;
-            a_pair(w0.x, w0.y, sel, sft, m8, a0, a1);
-            a_pair(w0.z, w0.w, sel, sft, m8, a2, a3);
-            mma_f16_16816(dq[0], a0, a1, a2, a3, b00, b01);
-            a_pair(w1.x, w1.y, sel, sft, m8, a0, a1);
-            a_pair(w1.z, w1.w, sel, sft, m8, a2, a3);
-            mma_f16_16816(dq[1], a0, a1, a2, a3, b10, b11);
+            mma_codes<false>(dq[0], w0.x, w0.y, w0.z, w0.w, sel, sft, m8, b00, b01);
+            mma_codes<false>(dq[1], w1.x, w1.y, w1.z, w1.w, sel, sft, m8, b10, b11);
         }
     }
     // this lane's half (gid&1), head tig: sum q'z - 4 sum q's
@@ -396,11 +409,8 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, i
                 const uint32_t w1 = q == 0 ? vv[1].x : q == 1 ? vv[1].y : q == 2 ? vv[1].z : vv[1].w;
                 const uint32_t w2 = q == 0 ? vv[2].x : q == 1 ? vv[2].y : q == 2 ? vv[2].z : vv[2].w;
                 const uint32_t w3 = q == 0 ? vv[3].x : q == 1 ? vv[3].y : q == 2 ? vv[3].z : vv[3].w;
-                uint32_t a0, a1, a2, a3;
-                a_pair(w0, w1, sel, sft, m8, a0, a1);
-                a_pair(w2, w3, sel, sft, m8, a2, a3);
-                if (kk == 0) mma_f16_16816_z(d[q], a0, a1, a2, a3, bw.x, bw.y);
-                else mma_f16_16816(d[q], a0, a1, a2, a3, bw.x, bw.y);
+                if (kk == 0) mma_codes<true>(d[q], w0, w1, w2, w3, sel, sft, m8, bw.x, bw.y);
+                else mma_codes<false>(d[q], w0, w1, w2, w3, sel, sft, m8, bw.x, bw.y);
             }
         }
 #pragma unroll
