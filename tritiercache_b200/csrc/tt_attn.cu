@@ -7,21 +7,22 @@
 //
 //   k_attn_partial  grid = (token chunks, jobs x kv-head groups), 8 warps.
 //     Each warp owns one kv head and walks 32-token units of its chunk:
-//       QK  lane <-> token.  Dense rows: FP32 dot with the G query heads of
-//           the kv head (GQA: every K byte is read once).  PBS rows: the
-//           block's 2-bit words are staged in shared memory and unpacked in
-//           registers; with qs = q*scale and F = 4 + code the score is
-//           sum(qs*F) - 4*sum(qs) + sum(q*zero) -- no dequantized copy.
-//       online softmax in log2 units (exp2), per-lane partial sums.
-//       PV  lane <-> channels.  Dense V rows are read coalesced; packed V
-//           words are unpacked in registers with the per-token scale folded
-//           into the weight (ws = p*scale) and the zero into a running sum.
+//       QK  Dense rows: FP32 dot with the G query heads of the kv head (GQA:
+//           every K byte is read once).  Packed rows: 2-bit codes used in
+//           place as 4 + code (tensor-core unit, tt_pbs_mma.cuh, or the SIMT
+//           unit): score = sum(q*scale*(4+code)) - 4 sum(q*scale) + sum(q*zero),
+//           no dequantized copy.
+//       online softmax in log2 units (exp2).
+//       PV  Dense V rows read coalesced; packed V codes with the per-token
+//           scale folded into the weight (p*scale) and the zero into a
+//           running sum.
 //     Output: per (chunk, q head) partial (m, l, acc[hd]) and the raw logits
 //     (for the mean attention weights).
-//   k_attn_finalize grid = (token ranges, jobs).  Log-sum-exp merge of the
-//     partials into attn_output, the head-mean softmax weights
-//     (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed score
-//     feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
+//   k_attn_merge_heads grid = (q heads, jobs).  Log-sum-exp merge of a head's
+//     chunk partials into attn_output, and the head's (M, 1/L).
+//   k_attn_weights grid = (positions / 256, jobs).  The head-mean softmax
+//     weights (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed
+//     score feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
 #include <algorithm>
 
 #include "tt_attn.cuh"
@@ -57,8 +58,118 @@ __device__ __forceinline__ void score_feedback(const JobDesc& J, const TierCount
     if (id >= 0 && id < J.msl) J.g[id] = fmaf(J.decay, J.g[id], w);
 }
 
-__global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ AttnLaunch L) {
-    extern __shared__ __align__(128) unsigned char smem[];
+// Weight of position pos averaged over heads: (1/nq) sum_h 2^(s_h - M_h) / L_h,
+// skipping -inf logits (16 heads' loads in flight per batch).
+__device__ __forceinline__ float mean_weight(const JobDesc& J, const float* Ms, const float* IL, int nq, int pos) {
+    const float* sc = J.scores;
+    const size_t stride = (size_t)J.score_stride;
+    float sw = 0.f;
+    int h = 0;
+    for (; h + 16 <= nq; h += 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (v[k] != -INFINITY) sw = fmaf(exp2f(v[k] - Ms[h + k]), IL[h + k], sw);
+    }
+    for (; h < nq; ++h) {
+        const float v = sc[(size_t)h * stride + pos];
+        if (v != -INFINITY) sw = fmaf(exp2f(v - Ms[h]), IL[h], sw);
+    }
+    return sw / (float)nq;
+}
+
+// (M, 1/L) of every head after k_attn_merge_heads: the partials' spare last
+// chunk slot (plans use at most max_chunks - 2 slots).
+__device__ __forceinline__ float* head_ml(const JobDesc& J) {
+    return J.part_ml + (size_t)(J.max_chunks - 1) * J.nq * 2;
+}
+
+// Merge of one head's chunk partials: M = max m, L = sum l 2^(m - M),
+// out = sum acc 2^(m - M) / L (row_sum_exp fallback, fused_attn_avx2.cpp:261).
+// grid (nq, njobs); warps split the chunks; dynamic shared memory:
+// (nd + np + 1 + NW * hd) floats.
+__global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__ AttnLaunch L) {
+    extern __shared__ float fsm[];
+    __shared__ JobDesc Js;
+    __shared__ TierCounts Ts;
+    __shared__ float red[NW];
+    __shared__ float Mh, Lh;
+    const int job = blockIdx.y, h = blockIdx.x;
+    if (threadIdx.x == 0) {
+        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
+        Ts = resolve_counts(Js);
+    }
+    __syncthreads();
+    const JobDesc& J = Js;
+    const TierCounts tc = Ts;
+    const int nq = J.nq, HD = J.hd;
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const int nd_act = ceil_div(D, L.DC), np_act = ceil_div(tc.nblk * J.grp, L.PC);
+    const int nch = nd_act + np_act;
+    float* wts = fsm;                        // [nch]
+    float* acc = fsm + L.nd + L.np + 1;      // [NW][HD]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto chunk_index = [&](int i) { return i < nd_act ? i : L.nd + (i - nd_act); };
+
+    float M = -INFINITY;
+    for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
+    M = warp_max(M);
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = red[0];
+        for (int w = 1; w < NW; ++w) m = fmaxf(m, red[w]);
+        Mh = m;
+    }
+    __syncthreads();
+    M = Mh;
+    float S = 0.f;
+    for (int i = threadIdx.x; i < nch; i += NT) {
+        const size_t pi = ((size_t)chunk_index(i) * nq + h) * 2;
+        const float mi = J.part_ml[pi];
+        const float w = (M == -INFINITY || mi == -INFINITY) ? 0.f : exp2f(mi - M);
+        wts[i] = w;
+        S = fmaf(J.part_ml[pi + 1], w, S);
+    }
+    S = warp_sum(S);
+    __syncthreads();
+    if (lane == 0) red[warp] = S;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < NW; ++w) t += red[w];
+        Lh = t;
+    }
+    __syncthreads();
+    // each warp sums a strided subset of the chunks over all channels
+    for (int c = lane; c < HD; c += 32) {
+        float o = 0.f;
+#pragma unroll 4
+        for (int i = warp; i < nch; i += NW) o = fmaf(J.part_acc[((size_t)chunk_index(i) * nq + h) * HD + c], wts[i], o);
+        acc[warp * HD + c] = o;
+    }
+    __syncthreads();
+    const float inv = 1.0f / (Lh > 0.f ? Lh : 1.0f);
+    float* out = L.out[job];
+    for (int c = threadIdx.x; c < HD; c += NT) {
+        float t = 0.f;
+        for (int w = 0; w < NW; ++w) t += acc[w * HD + c];
+        out[(size_t)h * HD + c] = t * inv;
+    }
+    if (threadIdx.x == 0) {
+        float* ml = head_ml(J);
+        ml[2 * h] = M;
+        ml[2 * h + 1] = inv;
+    }
+}
+
+// Mean attention weights over heads (fused_attn_avx2.cpp:286-300) and, for
+// engines, the score feedback; one position per thread.  grid (positions /
+// NT, njobs); dynamic shared memory: 2 nq floats.
+__global__ void __launch_bounds__(NT) k_attn_weights(const __grid_constant__ AttnLaunch L) {
+    extern __shared__ float fsm[];
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y;
@@ -69,119 +180,28 @@ __global__ void __launch_bounds__(NT) k_attn_finalize(const __grid_constant__ At
     __syncthreads();
     const JobDesc& J = Js;
     const TierCounts tc = Ts;
-    const int nq = J.nq, HD = J.hd;
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const int ntok = tc.nblk * J.grp;
-    const int T = D + ntok;
-    const int nd_act = ceil_div(D, L.DC), np_act = ceil_div(ntok, L.PC);
-    const int nch = nd_act + np_act;
-    float* Ms = reinterpret_cast<float*>(smem);   // [nq]
-    float* IL = Ms + nq;                          // [nq] 1 / L
-    float* wts = IL + nq;                         // [nch] merge weights of one head
-    float* red = wts + nch;                       // [NT] partial output sums
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto chunk_index = [&](int i) { return i < nd_act ? i : L.nd + (i - nd_act); };
-
-    // ---- global (M, L) per head from the chunk partials ----
-    for (int h = warp; h < nq; h += NW) {
-        float M = -INFINITY;
-        for (int i = lane; i < nch; i += 32) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
-        M = warp_max(M);
-        float S = 0.f;
-        if (M != -INFINITY) {
-            for (int i = lane; i < nch; i += 32) {
-                const size_t pi = ((size_t)chunk_index(i) * nq + h) * 2;
-                const float mi = J.part_ml[pi];
-                if (mi != -INFINITY) S = fmaf(J.part_ml[pi + 1], exp2f(mi - M), S);
-            }
-        }
-        S = warp_sum(S);
-        if (lane == 0) {
-            Ms[h] = M;
-            IL[h] = 1.0f / (S > 0.f ? S : 1.0f);  // row_sum_exp fallback (fused_attn_avx2.cpp:261)
-        }
+    const int nq = J.nq;
+    float* Ms = fsm;
+    float* IL = fsm + nq;
+    const float* ml = head_ml(J);
+    for (int h = threadIdx.x; h < nq; h += NT) {
+        Ms[h] = ml[2 * h];
+        IL[h] = ml[2 * h + 1];
     }
     __syncthreads();
-
-    // ---- attention output: heads blockIdx.x, blockIdx.x + nfin, ... ----
-    float* out = L.out[job];
-    const int groups = NT / HD > 0 ? NT / HD : 1;  // threads per channel
-    for (int h = blockIdx.x; h < nq; h += L.nfin) {
-        const float M = Ms[h], inv = IL[h];
-        for (int i = threadIdx.x; i < nch; i += NT) {
-            const float mi = J.part_ml[((size_t)chunk_index(i) * nq + h) * 2];
-            wts[i] = (M == -INFINITY || mi == -INFINITY) ? 0.f : exp2f(mi - M) * inv;
-        }
-        __syncthreads();
-        for (int c0 = 0; c0 < HD; c0 += NT) {
-            const int c = c0 + (threadIdx.x % HD), grp_i = threadIdx.x / HD;
-            float o = 0.f;
-            if (c < HD && grp_i < groups) {
-#pragma unroll 4
-                for (int i = grp_i; i < nch; i += groups)
-                    o = fmaf(J.part_acc[((size_t)chunk_index(i) * nq + h) * HD + c], wts[i], o);
-            }
-            red[threadIdx.x] = o;
-            __syncthreads();
-            if (threadIdx.x < HD && c0 + threadIdx.x < HD) {
-                float t = 0.f;
-                for (int k = 0; k < groups; ++k) t += red[k * HD + threadIdx.x];
-                out[(size_t)h * HD + c0 + threadIdx.x] = t;
-            }
-            __syncthreads();
-        }
-    }
-
-    // ---- mean attention weights over heads, score feedback ----
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const int T = D + tc.nblk * J.grp;
+    const int pos = blockIdx.x * NT + threadIdx.x;
+    if (pos >= T) return;
+    const float w = mean_weight(J, Ms, IL, nq, pos);
     float* mw = L.mw[job];
-    const int p0 = blockIdx.x * L.FT, p1 = min(T, p0 + L.FT);
-    const float* sc = J.scores;
-    const size_t stride = (size_t)J.score_stride;
-    for (int pos = p0 + threadIdx.x; pos < p1; pos += NT) {
-        float sw = 0.f;
-        int h = 0;
-        for (; h + 8 <= nq; h += 8) {
-            float v[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                if (v[k] != -INFINITY) sw = fmaf(exp2f(v[k] - Ms[h + k]), IL[h + k], sw);
-        }
-        for (; h < nq; ++h) {
-            const float v = sc[(size_t)h * stride + pos];
-            if (v != -INFINITY) sw = fmaf(exp2f(v - Ms[h]), IL[h], sw);
-        }
-        const float w = sw / (float)nq;
-        if (mw) mw[pos] = w;
-        if (J.g) score_feedback(J, tc, D, pos, w);
-    }
+    if (mw) mw[pos] = w;
+    if (J.g) score_feedback(J, tc, D, pos, w);
 }
 
 // ---------------------------------------------------------------------------
 // sequence-sharded attention (see launch_sharded_* in tt_attn.cuh)
 // ---------------------------------------------------------------------------
-// Sum of the positions' weights over heads / nq, as in k_attn_finalize.
-__device__ __forceinline__ float mean_weight(const JobDesc& J, const float* Ms, const float* IL, int nq, int pos) {
-    const float* sc = J.scores;
-    const size_t stride = (size_t)J.score_stride;
-    float sw = 0.f;
-    int h = 0;
-    for (; h + 8 <= nq; h += 8) {
-        float v[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-            if (v[k] != -INFINITY) sw = fmaf(exp2f(v[k] - Ms[h + k]), IL[h + k], sw);
-    }
-    for (; h < nq; ++h) {
-        const float v = sc[(size_t)h * stride + pos];
-        if (v != -INFINITY) sw = fmaf(exp2f(v - Ms[h]), IL[h], sw);
-    }
-    return sw / (float)nq;
-}
-
 // Position of local index i of a rank's share (dense positions first).
 __device__ __forceinline__ int shard_pos(const ShardRange& R, int D, int i) {
     const int nd = R.dhi - R.dlo;
@@ -379,8 +399,6 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
     L.PC = tokens(per_cta / pbs_tok, 64, 4096);
     L.nd = ceil_div(dense_cap, L.DC);
     L.np = ceil_div(pbs_tok_cap, L.PC);
-    L.FT = 1024;
-    L.nfin = std::max(1, ceil_div(dense_cap + pbs_tok_cap, L.FT));
     return TT_OK;
 }
 
@@ -470,18 +488,29 @@ tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int 
 }
 
 // L.inline_job.hd / .nq must be set for engine batches too (they select the
-// kernel instantiation and the finalize shared memory).
+// kernel instantiation and the merge shared memory).
 tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
     {
         tt_status s = launch_partial_any(L, st);
         if (s != TT_OK) return s;
     }
-    dim3 grid(L.nfin, L.njobs);
+    const int nq = L.inline_job.nq;
+    {
+        dim3 grid(nq, L.njobs);
+        const size_t sm = ((size_t)(L.nd + L.np + 1) + (size_t)NW * L.inline_job.hd) * sizeof(float);
+        const int ps = prof_begin(2, st);
+        k_attn_merge_heads<<<grid, NT, sm, st>>>(L);
+        prof_end(ps, st);
+        tt_status s = check_launch("k_attn_merge_heads");
+        if (s != TT_OK) return s;
+    }
+    // positions: at most nd * DC dense + np * PC packed
+    const long long tcap = (long long)L.nd * L.DC + (long long)L.np * L.PC;
+    dim3 grid((unsigned)std::max<long long>(1, (tcap + NT - 1) / NT), L.njobs);
     const int ps = prof_begin(2, st);
-    const size_t fsm = ((size_t)2 * L.inline_job.nq + (size_t)(L.nd + L.np) + NT) * sizeof(float);
-    k_attn_finalize<<<grid, NT, fsm, st>>>(L);
+    k_attn_weights<<<grid, NT, (size_t)2 * nq * sizeof(float), st>>>(L);
     prof_end(ps, st);
-    return check_launch("k_attn_finalize");
+    return check_launch("k_attn_weights");
 }
 
 // ---------------------------------------------------------------------------

@@ -85,8 +85,6 @@ struct AttnLaunch {
     int np;       // PBS chunk slots per job
     int DC;       // dense tokens per chunk (multiple of 32)
     int PC;       // PBS tokens per chunk (multiple of 32)
-    int FT;       // tokens per finalize CTA
-    int nfin;     // finalize CTAs per job
     int meta_bytes;  // largest PBS metadata element of the batch (2 or 4): sizes the staging buffers
     int rank, world; // sequence sharding: this launch attends only its share (world <= 1: everything)
     const JobDesc* jobs[kMaxBatch];  // device descriptor per job (engines) or nullptr
@@ -121,7 +119,7 @@ __host__ __device__ __forceinline__ ShardRange shard_range(int D, int nblk, int 
 }
 // Scratch a job needs for a given plan: chunk slots and score stride.
 int attn_max_chunks(int dense_cap, int pbs_tok_cap);
-// Launches the partial and finalize kernels on `stream`.
+// Launches the partial, head-merge and weights kernels on `stream`.
 tt_status launch_attention(const AttnLaunch& L, cudaStream_t stream);
 
 // Sequence-sharded attention, three stream-ordered phases around two

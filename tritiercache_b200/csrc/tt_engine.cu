@@ -10,10 +10,11 @@
 //                      strict-argmin replace with demotion), and flush a full
 //                      waiting room into one packed block (bit-exact
 //                      quantize+pack).  cache_engine.cpp:118-269, :397-431.
-//   k_attn_partial / k_attn_finalize (tt_attn.cu) over the tiers in place
-//                      (no dense re-assembly, cache_engine.cpp:433-459),
-//                      with the decayed score feedback fused into the
-//                      finalize pass (cache_engine.cpp:511-540).
+//   k_attn_partial / k_attn_merge_heads / k_attn_weights (tt_attn.cu) over
+//                      the tiers in place (no dense re-assembly,
+//                      cache_engine.cpp:433-459), with the decayed score
+//                      feedback fused into the weights pass
+//                      (cache_engine.cpp:511-540).
 // The host never waits for the device inside step(); the integer state the
 // host needs for grid sizing is either deterministic (token counts) or an
 // upper bound (packed blocks).

@@ -581,7 +581,7 @@ __device__ __forceinline__ void dense_unit(const JobDesc& J, const TierCounts& t
     __syncwarp();
     const int ntu = min(32, t1 - ub);
     const int c0 = lane * CPL;
-#pragma unroll 4
+#pragma unroll 16
     for (int t = 0; t < ntu; ++t) {
         const float* vr = vrow[t] + c0;
         const u64* wt = ws_tab + t * GM;
