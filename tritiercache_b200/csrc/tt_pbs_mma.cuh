@@ -220,20 +220,49 @@ __device__ __forceinline__ void mma_issue(const JobDesc& J, int kvh, int s0, int
     const char* vsb = reinterpret_cast<const char*>(J.vs) + soff;
     const char* vzb = reinterpret_cast<const char*>(J.vz) + soff;
     const char* ib = reinterpret_cast<const char*>(J.ids) + (size_t)s0 * 8;
-    const int rows = nt >> 4;
     const int krow = nkv * HD * 4;            // bytes between K word rows (16 tokens)
+    const int mblk = nkv * HD * 2;            // bytes between metadata blocks
+    const int vtok = nkv * DQ * 4;            // bytes between tokens' V words
+    if (nt == 32) {
+        // a full unit: every lane's pieces are fixed (straight-line issue)
+#pragma unroll
+        for (int j = 0; j < HD / 64; ++j) {  // K words: 2 rows x HD/4 chunks
+            const int i = lane + 32 * j, r = i / (HD / 4), c = i % (HD / 4);
+            cp_async16(st + SL::kw + r * HD * 4 + c * 16, kb + r * krow + c * 16);
+        }
+        if (gsh == 4 || lane < HD / 8) {  // K scale / zero: (32 >> gsh) blocks x HD/8 chunks
+            const int b = lane / (HD / 8), c = lane % (HD / 8);
+            if (HD == 64) {  // 8 chunks per block: lanes 0..15 cover both blocks
+                if (lane < (32 >> gsh) * (HD / 8)) {
+                    cp_async16(st + SL::ks + b * HD * 2 + c * 16, sb + b * mblk + c * 16);
+                    cp_async16(st + SL::kz + b * HD * 2 + c * 16, zb + b * mblk + c * 16);
+                }
+            } else {
+                cp_async16(st + SL::ks + b * HD * 2 + c * 16, sb + b * mblk + c * 16);
+                cp_async16(st + SL::kz + b * HD * 2 + c * 16, zb + b * mblk + c * 16);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < HD / 64; ++j) {  // V words: 32 tokens x HD/64 chunks
+            const int i = lane + 32 * j, t = i / (HD / 64), c = i % (HD / 64);
+            cp_async16(st + SL::vw + t * DQ * 4 + c * 16, vb + t * vtok + c * 16);
+        }
+        cp_async4(st + SL::vs + lane * 4, vsb + lane * nkv * 2);
+        cp_async4(st + SL::vz + lane * 4, vzb + lane * nkv * 2);
+        if (lane < 16) cp_async16(st + SL::ids + lane * 16, ib + lane * 16);
+        return;
+    }
+    const int rows = nt >> 4;
     for (int i = lane; i < rows * (HD / 4); i += 32) {  // K words: HD/4 chunks per row
         const int r = i / (HD / 4), c = i % (HD / 4);
         cp_async16(st + SL::kw + r * HD * 4 + c * 16, kb + r * krow + c * 16);
     }
     const int nb = max(1, nt >> gsh);
-    const int mblk = nkv * HD * 2;            // bytes between metadata blocks
     for (int i = lane; i < nb * (HD / 8); i += 32) {  // K scale / zero: HD/8 chunks per block
         const int b = i / (HD / 8), c = i % (HD / 8);
         cp_async16(st + SL::ks + b * HD * 2 + c * 16, sb + b * mblk + c * 16);
         cp_async16(st + SL::kz + b * HD * 2 + c * 16, zb + b * mblk + c * 16);
     }
-    const int vtok = nkv * DQ * 4;            // bytes between tokens' V words
     for (int i = lane; i < nt * (HD / 64); i += 32) {  // V words: HD/64 chunks per token
         const int t = i / (HD / 64), c = i % (HD / 64);
         cp_async16(st + SL::vw + t * DQ * 4 + c * 16, vb + t * vtok + c * 16);
