@@ -58,24 +58,30 @@ __device__ __forceinline__ void score_feedback(const JobDesc& J, const TierCount
     if (id >= 0 && id < J.msl) J.g[id] = fmaf(J.decay, J.g[id], w);
 }
 
+__device__ __forceinline__ float ex2_fast(float x) {  // 2^x, PTX ex2.approx (rel. error ~2^-22; -inf -> 0)
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Weight of position pos averaged over heads: (1/nq) sum_h 2^(s_h - M_h) / L_h,
-// skipping -inf logits (16 heads' loads in flight per batch).
+// skipping -inf logits.
 __device__ __forceinline__ float mean_weight(const JobDesc& J, const float* Ms, const float* IL, int nq, int pos) {
     const float* sc = J.scores;
     const size_t stride = (size_t)J.score_stride;
     float sw = 0.f;
     int h = 0;
-    for (; h + 16 <= nq; h += 16) {
-        float v[16];
+    for (; h + 32 <= nq; h += 32) {  // all 32 loads in flight before the first use
+        float v[32];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
+        for (int k = 0; k < 32; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-            if (v[k] != -INFINITY) sw = fmaf(exp2f(v[k] - Ms[h + k]), IL[h + k], sw);
+        for (int k = 0; k < 32; ++k)
+            if (v[k] != -INFINITY) sw = fmaf(ex2_fast(v[k] - Ms[h + k]), IL[h + k], sw);
     }
     for (; h < nq; ++h) {
         const float v = sc[(size_t)h * stride + pos];
-        if (v != -INFINITY) sw = fmaf(exp2f(v - Ms[h]), IL[h], sw);
+        if (v != -INFINITY) sw = fmaf(ex2_fast(v - Ms[h]), IL[h], sw);
     }
     return sw / (float)nq;
 }
