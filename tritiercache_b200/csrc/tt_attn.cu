@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__
     float* wts = fsm;                        // [nch]
     float* acc = fsm + L.nd + L.np + 1;      // [NW][HD]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto chunk_index = [&](int i) { return i < nd_act ? i : L.nd + (i - nd_act); };
+    auto chunk_index = [](int i) { return i; };  // compact partial slots, dense chunks first
 
     float M = -INFINITY;
     for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant_
     const int nd_act = ceil_div(R.dhi - R.dlo, L.DC), np_act = ceil_div(R.phi - R.plo, L.PC);
     const int nch = nd_act + np_act;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto chunk_index = [&](int i) { return i < nd_act ? i : L.nd + (i - nd_act); };
+    auto chunk_index = [](int i) { return i; };  // compact partial slots, dense chunks first
 
     float M = -INFINITY;
     for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
@@ -465,8 +465,24 @@ static tt_status launch_partial_any(const AttnLaunch& L, cudaStream_t st) {
     }
 }
 
+// The partial kernel merges a job's chunks in its last CTA when the caller
+// allows it and a job has few chunk slots (the merging CTA walks them alone;
+// wide single-job launches keep the nq-CTA merge kernel).
+constexpr int kTailMergeMaxChunks = 64;
+static bool tail_merge(const AttnLaunch& L) {
+    return L.merge_mode != 0 && L.nd + L.np > 0 && L.nd + L.np <= kTailMergeMaxChunks;
+}
+
 tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t st) {
-    tt_status s = launch_partial_any(L, st);
+    if (tail_merge(L)) {
+        AttnLaunch Lm = L;
+        Lm.merge_mode = 2;
+        Lm.xch = xch;
+        return launch_partial_any(Lm, st);
+    }
+    AttnLaunch L0 = L;
+    L0.merge_mode = 0;
+    tt_status s = launch_partial_any(L0, st);
     if (s != TT_OK) return s;
     dim3 grid(L.inline_job.nq, L.njobs);
     const int ps = prof_begin(2, st);  // the sharded epilogue kernels count as finalize
@@ -496,12 +512,15 @@ tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int 
 // L.inline_job.hd / .nq must be set for engine batches too (they select the
 // kernel instantiation and the merge shared memory).
 tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
+    const bool fused = tail_merge(L);
     {
-        tt_status s = launch_partial_any(L, st);
+        AttnLaunch Lp = L;
+        Lp.merge_mode = fused ? 1 : 0;
+        tt_status s = launch_partial_any(Lp, st);
         if (s != TT_OK) return s;
     }
     const int nq = L.inline_job.nq;
-    {
+    if (!fused) {
         dim3 grid(nq, L.njobs);
         const size_t sm = ((size_t)(L.nd + L.np + 1) + (size_t)NW * L.inline_job.hd) * sizeof(float);
         const int ps = prof_begin(2, st);

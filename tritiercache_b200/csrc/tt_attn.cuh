@@ -87,6 +87,12 @@ struct AttnLaunch {
     int PC;       // PBS tokens per chunk (multiple of 32)
     int meta_bytes;  // largest PBS metadata element of the batch (2 or 4): sizes the staging buffers
     int rank, world; // sequence sharding: this launch attends only its share (world <= 1: everything)
+    // merge_mode: the last partial CTA of each job merges the job's chunks
+    // (0 no: separate merge kernel; 1 -> out + (M, 1/L); 2 -> xch rows).  Callers
+    // set 1 to allow it (only engines: their per-job arrival counters start at
+    // zero); the launch functions pick the mode per launch.
+    int merge_mode;
+    float* xch;      // merge_mode 2: [njobs][nq][hd + 2] (m, l, acc) rows
     const JobDesc* jobs[kMaxBatch];  // device descriptor per job (engines) or nullptr
     JobDesc inline_job;              // stand-alone job (jobs[0] == nullptr, njobs == 1)
     const float* Q[kMaxBatch];

@@ -443,7 +443,7 @@ tt_status write_descriptors(tt_engine* e) {
     j.max_chunks = maxch;
     j.score_stride = dense_cap(e) + e->pbs_cap * e->chunk;
     j.part_ml = e->scratch;
-    j.part_acc = e->scratch + (size_t)maxch * j.nq * 2;
+    j.part_acc = e->scratch + ((size_t)maxch * j.nq * 2 + 3) / 4 * 4;  // 16-byte aligned (float4 reads)
     j.scores = j.part_acc + (size_t)maxch * j.nq * j.hd;
     j.g = e->g; j.hh_scores = e->HH_scores; j.hh_ids = e->HH_ids; j.decay = e->cfg.score_decay;
     j.msl = e->cfg.max_seq_len;
@@ -498,7 +498,12 @@ tt_status grow_pbs(tt_engine* e, int blocks) {
         e->scratch_floats = need;
     }
     if ((s = check_launch("PBS id init")) != TT_OK) return s;
-    return write_descriptors(e);
+    // the chunk-slot layout follows the capacity: start from a zeroed scratch
+    // (the attention kernel's per-job arrival counter must read 0)
+    if ((s = check_cuda(cudaMemset(e->scratch, 0, e->scratch_floats * sizeof(float)), "scratch clear")) != TT_OK)
+        return s;
+    if ((s = write_descriptors(e)) != TT_OK) return s;
+    return check_cuda(cudaDeviceSynchronize(), "PBS growth");
 }
 
 // Makes sure a step (extra_tokens = 1) or a prefill cannot run out of packed blocks.
@@ -621,6 +626,9 @@ tt_status validate_step(tt_engine* const* engines, int n, const float* const* Q,
             return set_error(TT_ERR_INVALID_ARGUMENT, "batched engines must share heads, head_dim and device.");
         if (((uintptr_t)Q[i] & 15) || ((uintptr_t)K_new[i] & 15) || ((uintptr_t)V_new[i] & 15))
             return set_error(TT_ERR_INVALID_ARGUMENT, "Q, K_new and V_new must be 16-byte aligned.");
+        for (int k = 0; k < i; ++k)
+            if (engines[k] == engines[i])
+                return set_error(TT_ERR_INVALID_ARGUMENT, "an engine appears more than once in one step.");
     }
     return TT_OK;
 }
@@ -740,6 +748,7 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
         s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, dcap, pcap);
         if (s != TT_OK) return s;
         fill_launch(L, engines + base, m, Q + base, attn_output + base);
+        L.merge_mode = 1;
         s = launch_attention(L, st);
         if (s != TT_OK) return s;
         advance_mirrors(engines + base, m, st);
@@ -791,6 +800,7 @@ tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const f
     fill_launch(L, engines, n, Q, nullptr);
     L.rank = rank;
     L.world = world;
+    L.merge_mode = 1;
     s = launch_sharded_partial(L, xch_send, st);
     if (s != TT_OK) return s;
     advance_mirrors(engines, n, st);

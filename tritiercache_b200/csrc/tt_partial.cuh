@@ -685,24 +685,15 @@ __host__ __device__ __forceinline__ size_t kernel_smem_bytes(int HG, int mb) {
 // even number of kv heads, fp16 metadata: the host only selects it then);
 // dense chunks are unchanged.
 template <int HD, int GM, bool MMA>
-__global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __grid_constant__ AttnLaunch L) {
+__device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc& J, const TierCounts tc) {
     constexpr int CPL = HDT<HD>::CPL;
     constexpr int NS = NSTAGE;  // stage slots of SIMT packed chunks
     using WA = WarpArea<HD, GM, MMA>;
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ JobDesc Js;
-    __shared__ TierCounts Ts;
     __shared__ __align__(8) uint64_t bars[NS];
 
     const int job = blockIdx.y / L.nhg;
     const int hg = blockIdx.y - job * L.nhg;
-    if (threadIdx.x == 0) {
-        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
-        Ts = resolve_counts(Js);
-    }
-    __syncthreads();
-    const JobDesc& J = Js;
-    const TierCounts tc = Ts;
     const int D = tc.n0 + tc.n1 + tc.n2;
     // this launch's share of the positions (all of them unless sharded)
     const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
@@ -754,7 +745,9 @@ __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __gr
     }
     __syncthreads();
     const float* qk = q_s + (size_t)kvl * GM * HD;
-    const int chunk = blockIdx.x;
+    // partial slot: this job's active chunks, dense first, packed after (compact,
+    // so a job's slots never depend on the other jobs of a batch)
+    const int chunk = is_dense ? (int)blockIdx.x : ceil_div(R.dhi - R.dlo, L.DC) + ((int)blockIdx.x - L.nd);
     float* mbuf = reinterpret_cast<float*>(smem + qbytes);  // merge buffer (aliases the stages / warp areas)
 
     if (MMA && !is_dense) {
@@ -923,6 +916,127 @@ __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __gr
     __syncthreads();
     if (r0 != 0 || !active) return;
     merge_warps<HD, GM>(J, mbuf, chunk, kvh, kvl, HG, WPH, G, lane);
+}
+
+// Arrival counter of a job's partial CTAs: the partials' spare chunk slot
+// max_chunks - 2 (a job's active chunks use at most max_chunks - 2 slots).
+// Zero between launches: the engine clears its scratch when it (re)sizes it
+// and the merging CTA resets the counter.
+__device__ __forceinline__ int* job_counter(const JobDesc& J) {
+    return reinterpret_cast<int*>(J.part_ml + (size_t)(J.max_chunks - 2) * J.nq * 2);
+}
+
+// After the CTA's own chunk: the last CTA of its job merges the job's chunk
+// partials per head -- M = max m, L = sum l 2^(m - M), acc = sum acc 2^(m - M)
+// (row_sum_exp fallback, fused_attn_avx2.cpp:261) -- into attn_output and
+// (M, 1/L) (merge_mode 1, what k_attn_merge_heads computes) or into the job's
+// exchange row (merge_mode 2, what k_shard_local_merge computes).  TPH threads
+// per head, each owning float4 channel groups, with many chunks' loads in
+// flight.  Release / acquire as in a grid barrier: CTA barrier, then one
+// thread fences and arrives; the merging CTA fences after the last arrival and
+// reads the partials through L2.
+template <int HD>
+__device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobDesc& J, const TierCounts tc) {
+    constexpr int TPH = HD >= 32 ? 8 : 4;      // threads per head
+    constexpr int V4 = HD / (4 * TPH);         // float4 groups per thread (channels 4 (tq + TPH v) ..)
+    constexpr int HPP = NT / TPH;              // heads per pass
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(job_counter(J), 1) == (int)(gridDim.x * L.nhg) - 1;
+        if (last) __threadfence();
+    }
+    __syncthreads();
+    if (!last) return;
+    const int job = blockIdx.y / L.nhg;
+    const int nq = J.nq;
+    const int D = tc.n0 + tc.n1 + tc.n2;
+    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
+    const int nch = ceil_div(R.dhi - R.dlo, L.DC) + ceil_div(R.phi - R.plo, L.PC);
+    const int tq = threadIdx.x % TPH;
+    const float2* pml = reinterpret_cast<const float2*>(J.part_ml);
+    for (int h = threadIdx.x / TPH; h < nq; h += HPP) {  // the TPH threads of a head are adjacent lanes
+        float M = -INFINITY;
+        for (int i = tq; i < nch; i += TPH) M = fmaxf(M, __ldcg(&pml[(size_t)i * nq + h].x));
+#pragma unroll
+        for (int x = 1; x < TPH; x <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+        float S = 0.f;
+        float4 o[V4];
+#pragma unroll
+        for (int v = 0; v < V4; ++v) o[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+        for (int i = 0; i < nch; ++i) {
+            const float2 p = __ldcg(&pml[(size_t)i * nq + h]);
+            const float w = (M == -INFINITY || p.x == -INFINITY) ? 0.f : exp2f(p.x - M);
+            S = fmaf(p.y, w, S);
+            const float4* a = reinterpret_cast<const float4*>(J.part_acc + ((size_t)i * nq + h) * HD) + tq;
+#pragma unroll
+            for (int v = 0; v < V4; ++v) {
+                const float4 x = __ldcg(a + TPH * v);
+                o[v].x = fmaf(x.x, w, o[v].x);
+                o[v].y = fmaf(x.y, w, o[v].y);
+                o[v].z = fmaf(x.z, w, o[v].z);
+                o[v].w = fmaf(x.w, w, o[v].w);
+            }
+        }
+        if (L.merge_mode == 2) {
+            float* xr = L.xch + ((size_t)job * nq + h) * (HD + 2);
+#pragma unroll
+            for (int v = 0; v < V4; ++v) {
+                const int c = 4 * (tq + TPH * v);
+                xr[2 + c] = o[v].x;
+                xr[3 + c] = o[v].y;
+                xr[4 + c] = o[v].z;
+                xr[5 + c] = o[v].w;
+            }
+            if (tq == 0) {
+                xr[0] = M;
+                xr[1] = S;
+            }
+        } else {
+            const float inv = 1.0f / (S > 0.f ? S : 1.0f);
+            float* out = L.out[job] + (size_t)h * HD;
+            if ((reinterpret_cast<uintptr_t>(L.out[job]) & 15) == 0) {
+#pragma unroll
+                for (int v = 0; v < V4; ++v)
+                    reinterpret_cast<float4*>(out)[tq + TPH * v] =
+                        make_float4(o[v].x * inv, o[v].y * inv, o[v].z * inv, o[v].w * inv);
+            } else {  // attn_output need not be 16-byte aligned
+#pragma unroll
+                for (int v = 0; v < V4; ++v) {
+                    const int c = 4 * (tq + TPH * v);
+                    out[c] = o[v].x * inv;
+                    out[c + 1] = o[v].y * inv;
+                    out[c + 2] = o[v].z * inv;
+                    out[c + 3] = o[v].w * inv;
+                }
+            }
+            if (tq == 0) {
+                float* ml = J.part_ml + (size_t)(J.max_chunks - 1) * nq * 2;  // (M, 1/L) for the weights pass
+                ml[2 * h] = M;
+                ml[2 * h + 1] = inv;
+            }
+        }
+    }
+    if (threadIdx.x == 0) *job_counter(J) = 0;
+}
+
+// grid (nd + np, njobs * nhg).  With merge_mode set, the job's last CTA also
+// merges the job's chunks (chunk_merge_tail); every CTA arrives, also those
+// without tokens.
+template <int HD, int GM, bool MMA>
+__global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __grid_constant__ AttnLaunch L) {
+    __shared__ JobDesc Js;
+    __shared__ TierCounts Ts;
+    if (threadIdx.x == 0) {
+        const int job = blockIdx.y / L.nhg;
+        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
+        Ts = resolve_counts(Js);
+    }
+    __syncthreads();
+    partial_body<HD, GM, MMA>(L, Js, Ts);
+    if (L.merge_mode) chunk_merge_tail<HD>(L, Js, Ts);
 }
 
 }  // namespace tt
