@@ -391,12 +391,15 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
         return set_error(TT_ERR_UNSUPPORTED, "num_kv_heads > 8 must be a multiple of 8 (got %d).", nkv);
     }
     L.nhg = nkv / L.HG;
-    // Chunks are sized by bytes: a dense FP32 token moves ~10x the bytes of a
-    // packed one.  Aim for about four CTAs of work per SM over the launch.
+    // Chunks are sized by estimated time: a token's bytes (a dense FP32 token
+    // moves ~10x the bytes of a packed one), packed bytes weighted 1.4x for
+    // their lower streaming rate.  About twelve CTAs of work per SM (six waves
+    // at two resident CTAs): the block scheduler then balances dense against
+    // packed chunks and the last partial wave is short.
     const double dense_tok = (double)L.HG * hd * 8.0;
-    const double pbs_tok = (double)L.HG * (hd / 2.0 + 2.0 * hd * 4 / 16.0 + 8.0) + 8.0;
+    const double pbs_tok = 1.4 * ((double)L.HG * (hd / 2.0 + 2.0 * hd * 4 / 16.0 + 8.0) + 8.0);
     const double total = (double)L.njobs * L.nhg * (dense_cap * dense_tok + pbs_tok_cap * pbs_tok);
-    const double per_cta = std::max(total / (4.0 * 148.0), 1.0);
+    const double per_cta = std::max(total / (12.0 * 148.0), 1.0);
     auto tokens = [](double t, long long lo, long long hi) {
         long long c = ((long long)t + 31) / 32 * 32;
         return (int)std::max(lo, std::min(hi, c));
@@ -468,7 +471,7 @@ static tt_status launch_partial_any(const AttnLaunch& L, cudaStream_t st) {
 // The partial kernel merges a job's chunks in its last CTA when the caller
 // allows it and a job has few chunk slots (the merging CTA walks them alone;
 // wide single-job launches keep the nq-CTA merge kernel).
-constexpr int kTailMergeMaxChunks = 64;
+constexpr int kTailMergeMaxChunks = 128;
 static bool tail_merge(const AttnLaunch& L) {
     return L.merge_mode != 0 && L.nd + L.np > 0 && L.nd + L.np <= kTailMergeMaxChunks;
 }
