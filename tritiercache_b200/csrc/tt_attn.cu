@@ -34,64 +34,6 @@ namespace tt {
 // ---------------------------------------------------------------------------
 // merge + mean weights + score feedback
 // ---------------------------------------------------------------------------
-// g[id] = decay * g[id] + w for the token at position `pos` (cache_engine.cpp:511-540):
-// sinks, heavy hitters (whose HH_scores copy follows), the recent ring and the
-// packed tier; ids outside [0, max_seq_len) are skipped.
-__device__ __forceinline__ void score_feedback(const JobDesc& J, const TierCounts& tc, int D, int pos, float w) {
-    long long id;
-    if (pos < tc.n0) {
-        id = pos;
-    } else if (pos < tc.n0 + tc.n1) {
-        const int i = pos - tc.n0;
-        id = J.hh_ids[i];
-        if (id >= 0 && id < J.msl) {
-            const float nv = fmaf(J.decay, J.g[id], w);
-            J.g[id] = nv;
-            J.hh_scores[i] = nv;
-        }
-        return;
-    } else if (pos < D) {
-        id = (long long)tc.total - tc.n2 + (pos - tc.n0 - tc.n1);
-    } else {
-        id = J.ids[pos - D];
-    }
-    if (id >= 0 && id < J.msl) J.g[id] = fmaf(J.decay, J.g[id], w);
-}
-
-__device__ __forceinline__ float ex2_fast(float x) {  // 2^x, PTX ex2.approx (rel. error ~2^-22; -inf -> 0)
-    float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-
-// Weight of position pos averaged over heads: (1/nq) sum_h 2^(s_h - M_h) / L_h,
-// skipping -inf logits.
-__device__ __forceinline__ float mean_weight(const JobDesc& J, const float* Ms, const float* IL, int nq, int pos) {
-    const float* sc = J.scores;
-    const size_t stride = (size_t)J.score_stride;
-    float sw = 0.f;
-    int h = 0;
-    for (; h + 32 <= nq; h += 32) {  // all 32 loads in flight before the first use
-        float v[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = sc[(size_t)(h + k) * stride + pos];
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-            if (v[k] != -INFINITY) sw = fmaf(ex2_fast(v[k] - Ms[h + k]), IL[h + k], sw);
-    }
-    for (; h < nq; ++h) {
-        const float v = sc[(size_t)h * stride + pos];
-        if (v != -INFINITY) sw = fmaf(ex2_fast(v - Ms[h]), IL[h], sw);
-    }
-    return sw / (float)nq;
-}
-
-// (M, 1/L) of every head after k_attn_merge_heads: the partials' spare last
-// chunk slot (plans use at most max_chunks - 2 slots).
-__device__ __forceinline__ float* head_ml(const JobDesc& J) {
-    return J.part_ml + (size_t)(J.max_chunks - 1) * J.nq * 2;
-}
-
 // Merge of one head's chunk partials: M = max m, L = sum l 2^(m - M),
 // out = sum acc 2^(m - M) / L (row_sum_exp fallback, fused_attn_avx2.cpp:261).
 // grid (nq, njobs); warps split the chunks; dynamic shared memory:
@@ -172,9 +114,9 @@ __global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__
 }
 
 // Mean attention weights over heads (fused_attn_avx2.cpp:286-300) and, for
-// engines, the score feedback; one position per thread.  grid (positions /
-// NT, njobs); dynamic shared memory: 2 nq floats.
-__global__ void __launch_bounds__(NT) k_attn_weights(const __grid_constant__ AttnLaunch L) {
+// engines, the score feedback; one position per thread, CTAs stride over the
+// job's positions.  grid (gx, njobs); dynamic shared memory: 2 nq floats.
+__global__ void __launch_bounds__(NT, 4) k_attn_weights(const __grid_constant__ AttnLaunch L) {
     extern __shared__ float fsm[];
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
@@ -197,12 +139,8 @@ __global__ void __launch_bounds__(NT) k_attn_weights(const __grid_constant__ Att
     __syncthreads();
     const int D = tc.n0 + tc.n1 + tc.n2;
     const int T = D + tc.nblk * J.grp;
-    const int pos = blockIdx.x * NT + threadIdx.x;
-    if (pos >= T) return;
-    const float w = mean_weight(J, Ms, IL, nq, pos);
-    float* mw = L.mw[job];
-    if (mw) mw[pos] = w;
-    if (J.g) score_feedback(J, tc, D, pos, w);
+    for (int pos = blockIdx.x * NT + threadIdx.x; pos < T; pos += gridDim.x * NT)
+        weigh_position(J, tc, D, Ms, IL, L.mw[job], pos);
 }
 
 // ---------------------------------------------------------------------------
@@ -532,9 +470,12 @@ tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
         tt_status s = check_launch("k_attn_merge_heads");
         if (s != TT_OK) return s;
     }
-    // positions: at most nd * DC dense + np * PC packed
+    // positions: at most nd * DC dense + np * PC packed; about eight CTAs per
+    // SM over the launch (several waves of short CTAs: each thread's chain of
+    // dependent loads is short), each striding over its job's positions
     const long long tcap = (long long)L.nd * L.DC + (long long)L.np * L.PC;
-    dim3 grid((unsigned)std::max<long long>(1, (tcap + NT - 1) / NT), L.njobs);
+    const long long gx = std::min<long long>((tcap + NT - 1) / NT, std::max(1, 8 * 148 / L.njobs));
+    dim3 grid((unsigned)std::max<long long>(1, gx), L.njobs);
     const int ps = prof_begin(2, st);
     k_attn_weights<<<grid, NT, (size_t)2 * nq * sizeof(float), st>>>(L);
     prof_end(ps, st);

@@ -18,6 +18,7 @@
 //       zero/offset back in at the end.
 #pragma once
 #include "tt_attn.cuh"
+#include "tt_weights.cuh"
 
 namespace tt {
 
@@ -685,25 +686,25 @@ __host__ __device__ __forceinline__ size_t kernel_smem_bytes(int HG, int mb) {
 // even number of kv heads, fp16 metadata: the host only selects it then);
 // dense chunks are unchanged.
 template <int HD, int GM, bool MMA>
-__device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc& J, const TierCounts tc) {
+__device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc& J, const TierCounts tc, int bx, int by) {
     constexpr int CPL = HDT<HD>::CPL;
     constexpr int NS = NSTAGE;  // stage slots of SIMT packed chunks
     using WA = WarpArea<HD, GM, MMA>;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[NS];
 
-    const int job = blockIdx.y / L.nhg;
-    const int hg = blockIdx.y - job * L.nhg;
+    const int job = by / L.nhg;
+    const int hg = by - job * L.nhg;
     const int D = tc.n0 + tc.n1 + tc.n2;
     // this launch's share of the positions (all of them unless sharded)
     const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
-    const bool is_dense = (int)blockIdx.x < L.nd;
+    const bool is_dense = bx < L.nd;
     int t0, t1;
     if (is_dense) {
-        t0 = R.dlo + blockIdx.x * L.DC;
+        t0 = R.dlo + bx * L.DC;
         t1 = min(R.dhi, t0 + L.DC);
     } else {
-        t0 = R.plo + (blockIdx.x - L.nd) * L.PC;
+        t0 = R.plo + (bx - L.nd) * L.PC;
         t1 = min(R.phi, t0 + L.PC);
     }
     if (t0 >= t1) return;
@@ -747,7 +748,7 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
     const float* qk = q_s + (size_t)kvl * GM * HD;
     // partial slot: this job's active chunks, dense first, packed after (compact,
     // so a job's slots never depend on the other jobs of a batch)
-    const int chunk = is_dense ? (int)blockIdx.x : ceil_div(R.dhi - R.dlo, L.DC) + ((int)blockIdx.x - L.nd);
+    const int chunk = is_dense ? bx : ceil_div(R.dhi - R.dlo, L.DC) + (bx - L.nd);
     float* mbuf = reinterpret_cast<float*>(smem + qbytes);  // merge buffer (aliases the stages / warp areas)
 
     if (MMA && !is_dense) {
@@ -918,7 +919,7 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
     merge_warps<HD, GM>(J, mbuf, chunk, kvh, kvl, HG, WPH, G, lane);
 }
 
-// Arrival counter of a job's partial CTAs: the partials' spare chunk slot
+// Arrival counter of a job's chunk CTAs: the partials' spare chunk slot
 // max_chunks - 2 (a job's active chunks use at most max_chunks - 2 slots).
 // Zero between launches: the engine clears its scratch when it (re)sizes it
 // and the merging CTA resets the counter.
@@ -936,7 +937,7 @@ __device__ __forceinline__ int* job_counter(const JobDesc& J) {
 // thread fences and arrives; the merging CTA fences after the last arrival and
 // reads the partials through L2.
 template <int HD>
-__device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobDesc& J, const TierCounts tc) {
+__device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobDesc& J, const TierCounts tc, int job) {
     constexpr int TPH = HD >= 32 ? 8 : 4;      // threads per head
     constexpr int V4 = HD / (4 * TPH);         // float4 groups per thread (channels 4 (tq + TPH v) ..)
     constexpr int HPP = NT / TPH;              // heads per pass
@@ -944,12 +945,11 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        last = atomicAdd(job_counter(J), 1) == (int)(gridDim.x * L.nhg) - 1;
+        last = atomicAdd(job_counter(J), 1) == (L.nd + L.np) * L.nhg - 1;
         if (last) __threadfence();
     }
     __syncthreads();
     if (!last) return;
-    const int job = blockIdx.y / L.nhg;
     const int nq = J.nq;
     const int D = tc.n0 + tc.n1 + tc.n2;
     const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
@@ -1013,7 +1013,7 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
                 }
             }
             if (tq == 0) {
-                float* ml = J.part_ml + (size_t)(J.max_chunks - 1) * nq * 2;  // (M, 1/L) for the weights pass
+                float* ml = head_ml(J);  // (M, 1/L) for the weights pass
                 ml[2 * h] = M;
                 ml[2 * h + 1] = inv;
             }
@@ -1029,14 +1029,14 @@ template <int HD, int GM, bool MMA>
 __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __grid_constant__ AttnLaunch L) {
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
+    const int job = blockIdx.y / L.nhg;
     if (threadIdx.x == 0) {
-        const int job = blockIdx.y / L.nhg;
         Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
         Ts = resolve_counts(Js);
     }
     __syncthreads();
-    partial_body<HD, GM, MMA>(L, Js, Ts);
-    if (L.merge_mode) chunk_merge_tail<HD>(L, Js, Ts);
+    partial_body<HD, GM, MMA>(L, Js, Ts, blockIdx.x, blockIdx.y);
+    if (L.merge_mode) chunk_merge_tail<HD>(L, Js, Ts, job);
 }
 
 }  // namespace tt

@@ -315,9 +315,11 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, i
     float bd[4] = {0.f, 0.f, 0.f, 0.f};
     float dq[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     {
+        // the bias rows' scales are the B fragments' scales of block gid&1
+        // (sv0 / sv1 below); their zeros come with one 8-byte load
         const int mo = ((16 * (gid & 1)) >> gsh) * HD + 4 * tig;
-        const uint32_t* ms_row = reinterpret_cast<const uint32_t*>(ks_s + mo);
-        const uint32_t* mz_row = reinterpret_cast<const uint32_t*>(kz_s + mo);
+        const __half* mz_row = kz_s + mo;
+        const bool odd_blk = (gid & 1) != 0 && gsh == 4;
         const uint32_t* kw0 = kw_s + 4 * tig;
         const uint32_t* kw1 = kw0 + HD;
         const __half* sb0 = ks_s + 4 * tig;
@@ -327,17 +329,19 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, i
                                ((gid & 1) ? (gid >> 1) * 4 + tig : 16 + tig) * 2;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
-            mma_f16_16816(bd, ms_row[8 * ks], mz_row[8 * ks], ms_row[8 * ks + 1], mz_row[8 * ks + 1], Q.qx[ks][0],
-                          Q.qx[ks][1]);
             const uint4 w0 = *reinterpret_cast<const uint4*>(kw0 + 16 * ks);
             const uint4 w1 = *reinterpret_cast<const uint4*>(kw1 + 16 * ks);
             const uint2 sv0 = *reinterpret_cast<const uint2*>(sb0 + 16 * ks);
+            const uint2 zv = *reinterpret_cast<const uint2*>(mz_row + 16 * ks);
             const uint2 qm = *reinterpret_cast<const uint2*>(qm_t + ks * 40);
+            uint2 sv1 = sv0;
+            if (!shared_blk) sv1 = *reinterpret_cast<const uint2*>(sb1 + 16 * ks);
+            const uint2 svb = odd_blk ? sv1 : sv0;
+            mma_f16_16816(bd, svb.x, zv.x, svb.y, zv.y, Q.qx[ks][0], Q.qx[ks][1]);
             const uint32_t b00 = b_qs(qm.x, Q.qx[ks][0], sv0.x);
             const uint32_t b01 = b_qs(qm.y, Q.qx[ks][1], sv0.y);
             uint32_t b10 = b00, b11 = b01;
             if (!shared_blk) {
-                const uint2 sv1 = *reinterpret_cast<const uint2*>(sb1 + 16 * ks);
                 b10 = b_qs(qm.x, Q.qx[ks][0], sv1.x);
                 b11 = b_qs(qm.y, Q.qx[ks][1], sv1.y);
             }
@@ -348,13 +352,15 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, i
     // this lane's half (gid&1), head tig: sum q'z - 4 sum q's
     const float bias_own = (bd[2] + bd[3]) - 4.0f * (bd[0] + bd[1]);
     float s[4];  // unit-local tokens gid, gid+8, 16+gid, 24+gid; head tig
+    // live tokens of the unit (present and not tombstoned): one id per lane
+    const uint32_t live_mask = __ballot_sync(0xffffffffu, lane < nt && ids_s[lane] != -1);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
         const float bias = __shfl_sync(0xffffffffu, bias_own, 4 * hf + tig);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int t = 16 * hf + gid + 8 * j;
-            const bool live = (hf == 0 || two) && tig < G && ids_s[t] != -1;
+            const bool live = tig < G && ((live_mask >> t) & 1u);
             s[2 * hf + j] = live ? ((dq[hf][2 * j] + dq[hf][2 * j + 1]) + bias) * Q.up_sc : -INFINITY;
         }
     }
