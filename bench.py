@@ -367,18 +367,19 @@ def main():
     launches_per_step = (kt.maintain_launches + kt.partial_launches + kt.finalize_launches) / args.steps
 
     # ---- e2e through the public API with host buffers ----
-    hQ = torch.empty((L, nq * hd), pin_memory=True)
-    hK = torch.empty((L, nkv * hd), pin_memory=True)
-    hV = torch.empty((L, nkv * hd), pin_memory=True)
+    # one pinned host buffer per direction: [layer][Q | K_new | V_new] goes up in
+    # one copy, attn_output comes back in one
+    wq, wk = nq * hd, nkv * hd
+    hIn = torch.empty((L, wq + 2 * wk), pin_memory=True)
     hO = torch.empty((L, nq * hd), pin_memory=True)
-    hQ.copy_(Qs[0].cpu()); hK.copy_(Ks[0].cpu()); hV.copy_(Vs[0].cpu())
-    dQ, dK, dV = torch.empty_like(Qs[0]), torch.empty_like(Ks[0]), torch.empty_like(Vs[0])
+    hIn[:, :wq].copy_(Qs[0].cpu()); hIn[:, wq:wq + wk].copy_(Ks[0].cpu()); hIn[:, wq + wk:].copy_(Vs[0].cpu())
+    dIn = torch.empty((L, wq + 2 * wk), device="cuda")
+    dQ, dK, dV = list(dIn[:, :wq]), list(dIn[:, wq:wq + wk]), list(dIn[:, wq + wk:])
+    out_rows = list(out)
 
     def e2e_step():
-        dQ.copy_(hQ, non_blocking=True)
-        dK.copy_(hK, non_blocking=True)
-        dV.copy_(hV, non_blocking=True)
-        step_fn(engines, list(dQ), list(dK), list(dV), list(out))
+        dIn.copy_(hIn, non_blocking=True)
+        step_fn(engines, dQ, dK, dV, out_rows)
         hO.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -458,7 +459,7 @@ def main():
                                             "partial": round(kt.partial_ms / args.steps, 5),
                                             "finalize": round(kt.finalize_ms / args.steps, 5)}},
         "e2e": {"value": round(ms_e2e * 1000.0, 2), "unit": UNIT,
-                "h2d_bytes_per_step": int(hQ.numel() * 4 + hK.numel() * 4 + hV.numel() * 4),
+                "h2d_bytes_per_step": int(hIn.numel() * 4),
                 "d2h_bytes_per_step": int(hO.numel() * 4)},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clocks,
