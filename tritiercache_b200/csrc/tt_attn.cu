@@ -36,9 +36,13 @@ namespace tt {
 // ---------------------------------------------------------------------------
 // Merge of one head's chunk partials: M = max m, L = sum l 2^(m - M),
 // out = sum acc 2^(m - M) / L (row_sum_exp fallback, fused_attn_avx2.cpp:261).
-// grid (nq, njobs); warps split the chunks; dynamic shared memory:
-// (nd + np + 1 + NW * hd) floats.
-__global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__ AttnLaunch L) {
+// grid (nq, njobs, groups); warps split the chunks; dynamic shared memory:
+// (group + 1 + NW * hd) floats.  Jobs with many chunks merge in two passes:
+// pass 1 (final = 0) merges each group of `group` chunks into the group's
+// first slot, unnormalised; pass 2 (final = 1, stride = that group size)
+// merges the group results at slots 0, stride, 2 stride, ...
+__global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__ AttnLaunch L, int group, int stride,
+                                                         int final_pass) {
     extern __shared__ float fsm[];
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
@@ -55,11 +59,15 @@ __global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__
     const int nq = J.nq, HD = J.hd;
     const int D = tc.n0 + tc.n1 + tc.n2;
     const int nd_act = ceil_div(D, L.DC), np_act = ceil_div(tc.nblk * J.grp, L.PC);
-    const int nch = nd_act + np_act;
-    float* wts = fsm;                        // [nch]
-    float* acc = fsm + L.nd + L.np + 1;      // [NW][HD]
+    const int nch_all = ceil_div(nd_act + np_act, stride);  // entries of this pass
+    const int c0 = blockIdx.z * group;
+    const int nch = max(0, min(group, nch_all - c0));
+    if (!final_pass && nch == 0) return;
+    float* wts = fsm;                        // [group]
+    float* acc = fsm + group + 1;            // [NW][HD]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto chunk_index = [](int i) { return i; };  // compact partial slots, dense chunks first
+    // compact partial slots (dense chunks first), every stride-th in pass 2
+    auto chunk_index = [&](int i) { return (c0 + i) * stride; };
 
     float M = -INFINITY;
     for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
@@ -98,7 +106,20 @@ __global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__
         for (int i = warp; i < nch; i += NW) o = fmaf(J.part_acc[((size_t)chunk_index(i) * nq + h) * HD + c], wts[i], o);
         acc[warp * HD + c] = o;
     }
-    __syncthreads();
+    __syncthreads();  // every read of this group's slots is done before the first slot is overwritten
+    if (!final_pass) {
+        const size_t pi = (size_t)chunk_index(0) * nq + h;
+        for (int c = threadIdx.x; c < HD; c += NT) {
+            float t = 0.f;
+            for (int w = 0; w < NW; ++w) t += acc[w * HD + c];
+            J.part_acc[pi * HD + c] = t;
+        }
+        if (threadIdx.x == 0) {
+            J.part_ml[pi * 2] = M;
+            J.part_ml[pi * 2 + 1] = Lh;
+        }
+        return;
+    }
     const float inv = 1.0f / (Lh > 0.f ? Lh : 1.0f);
     float* out = L.out[job];
     for (int c = threadIdx.x; c < HD; c += NT) {
@@ -410,6 +431,7 @@ static tt_status launch_partial_any(const AttnLaunch& L, cudaStream_t st) {
 // allows it and a job has few chunk slots (the merging CTA walks them alone;
 // wide single-job launches keep the nq-CTA merge kernel).
 constexpr int kTailMergeMaxChunks = 128;
+constexpr int kMergeGroup = 64;  // chunk slots per CTA of the separate head merge
 static bool tail_merge(const AttnLaunch& L) {
     return L.merge_mode != 0 && L.nd + L.np > 0 && L.nd + L.np <= kTailMergeMaxChunks;
 }
@@ -462,10 +484,18 @@ tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
     }
     const int nq = L.inline_job.nq;
     if (!fused) {
-        dim3 grid(nq, L.njobs);
-        const size_t sm = ((size_t)(L.nd + L.np + 1) + (size_t)NW * L.inline_job.hd) * sizeof(float);
+        // up to kMergeGroup chunk slots per job in one pass, else two
+        const int nch = L.nd + L.np;
+        const int groups = ceil_div(nch, kMergeGroup);
+        const size_t sm = ((size_t)std::max(kMergeGroup, groups) + 1 + (size_t)NW * L.inline_job.hd) * sizeof(float);
         const int ps = prof_begin(2, st);
-        k_attn_merge_heads<<<grid, NT, sm, st>>>(L);
+        if (groups > 1) {
+            k_attn_merge_heads<<<dim3(nq, L.njobs, groups), NT, sm, st>>>(L, kMergeGroup, 1, 0);
+            tt_status s = check_launch("k_attn_merge_heads");
+            if (s != TT_OK) return s;
+        }
+        k_attn_merge_heads<<<dim3(nq, L.njobs, 1), NT, sm, st>>>(L, groups > 1 ? groups : nch,
+                                                                   groups > 1 ? kMergeGroup : 1, 1);
         prof_end(ps, st);
         tt_status s = check_launch("k_attn_merge_heads");
         if (s != TT_OK) return s;
