@@ -13,7 +13,9 @@ the reference measures its kernels on synthetic tensors too.
 A "step" is one decode step of all 32 layers through the engine: ingest the
 new token (ring insert / evict / route / waiting-room flush), fused attention
 over every tier, decayed score feedback -- three kernel launches for the 32
-layers (k_engine_maintain, k_attn_partial, k_attn_finalize).
+layers (k_engine_maintain, k_attn_partial whose last CTA per layer merges the
+layer's chunks, k_attn_weights); the "finalize" time is the launches after the
+partial kernel.
 The per-step inputs are 1.3 GB of KV tiers, far larger than the 126 MB L2.
 
   value : device time per step (CUDA events, inputs resident in HBM), max over ranks.
