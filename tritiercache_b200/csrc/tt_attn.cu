@@ -142,22 +142,21 @@ __global__ void __launch_bounds__(NT, 4) k_attn_weights(const __grid_constant__ 
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y;
-    if (threadIdx.x == 0) {
-        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
-        Ts = resolve_counts(Js);
-    }
+    if (threadIdx.x == 0) Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
     __syncthreads();
     const JobDesc& J = Js;
-    const TierCounts tc = Ts;
     const int nq = J.nq;
     float* Ms = fsm;
     float* IL = fsm + nq;
+    // the heads' (M, 1/L) and the tier counters are independent loads: one round trip
+    if (threadIdx.x == 0) Ts = resolve_counts(J);
     const float* ml = head_ml(J);
     for (int h = threadIdx.x; h < nq; h += NT) {
         Ms[h] = ml[2 * h];
         IL[h] = ml[2 * h + 1];
     }
     __syncthreads();
+    const TierCounts tc = Ts;
     const int D = tc.n0 + tc.n1 + tc.n2;
     const int T = D + tc.nblk * J.grp;
     for (int pos = blockIdx.x * NT + threadIdx.x; pos < T; pos += gridDim.x * NT)
@@ -248,13 +247,10 @@ __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ Attn
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y;
-    if (threadIdx.x == 0) {
-        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
-        Ts = resolve_counts(Js);
-    }
+    if (threadIdx.x == 0) Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
     __syncthreads();
     const JobDesc& J = Js;
-    const TierCounts tc = Ts;
+    if (threadIdx.x == 0) Ts = resolve_counts(J);  // overlaps the row reads below
     const int nq = J.nq, HD = J.hd, P = L.world;
     float* Ms = sm;
     float* IL = sm + nq;
@@ -278,6 +274,7 @@ __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ Attn
         }
     }
     __syncthreads();
+    const TierCounts tc = Ts;
     float* out = L.out[job];
     for (int h = blockIdx.x; h < nq; h += gridDim.x) {
         const float M = Ms[h], inv = IL[h];
@@ -305,6 +302,9 @@ __global__ void __launch_bounds__(NT) k_shard_feedback(const __grid_constant__ A
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y, p = blockIdx.z;
+    const int i = blockIdx.x * NT + threadIdx.x;
+    // the weight does not depend on the descriptor chain: load it first
+    const float w = i < slot_cap ? mw_all[((size_t)p * L.njobs + job) * slot_cap + i] : 0.f;
     if (threadIdx.x == 0) {
         Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
         Ts = resolve_counts(Js);
@@ -316,9 +316,8 @@ __global__ void __launch_bounds__(NT) k_shard_feedback(const __grid_constant__ A
     const int D = tc.n0 + tc.n1 + tc.n2;
     const ShardRange R = shard_range(D, tc.nblk, J.grp, p, L.world);
     const int n_loc = (R.dhi - R.dlo) + (R.phi - R.plo);
-    const int i = blockIdx.x * NT + threadIdx.x;
     if (i >= n_loc || i >= slot_cap) return;
-    score_feedback(J, tc, D, shard_pos(R, D, i), mw_all[((size_t)p * L.njobs + job) * slot_cap + i]);
+    score_feedback(J, tc, D, shard_pos(R, D, i), w);
 }
 
 // ---------------------------------------------------------------------------
