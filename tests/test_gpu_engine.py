@@ -178,6 +178,33 @@ def test_engine_argument_errors(C_):
         e.step(None, None, None, None)
 
 
+def test_batched_step_rejects_an_engine_listed_twice_and_keeps_working(C_):
+    """One engine twice in one step would run its maintenance twice and break the
+    per-layer arrival counter of the fused merge: the step is refused before any
+    launch, and the engine's next step still matches the oracle."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(7)
+    nq, nkv, hd = 4, 2, 64
+    eo = O.Engine(nq, nkv, hd, 256, 4, 16, 0.1, 0.999, 16, 16, "fp16")
+    eg = C_.TriTierCacheEngine(nq, nkv, hd, 256, 4, 16, 0.1, 0.999, 16, 16, "fp16")
+    K = rng.standard_normal((96, nkv, hd)).astype(np.float32)
+    V = rng.standard_normal((96, nkv, hd)).astype(np.float32)
+    eo.prefill(K, V, 96)
+    eg.prefill(K, V, 96)
+    q, k, v = (torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda() for n in (nq * hd, nkv * hd, nkv * hd))
+    o1, o2 = torch.zeros(nq * hd, device="cuda"), torch.zeros(nq * hd, device="cuda")
+    with pytest.raises(ValueError):
+        C_.engine_step_batched([eg, eg], [q, q], [k, k], [v, v], [o1, o2])
+    assert eg.counters()["total_processed_tokens"] == eo.counters()["total_processed_tokens"]
+    out_o = np.zeros(nq * hd, np.float32)
+    eo.step(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), out_o)
+    C_.engine_step_batched([eg], [q], [k], [v], [o1])
+    torch.cuda.synchronize()
+    ok, err = close(o1.cpu().numpy(), out_o)
+    assert ok, err
+    compare_state(eo, eg, "after the refused step")
+
+
 def test_engine_properties_and_buffer_bytes_match_reference_formula(C_):
     from oracle import oracle as O
     for meta, grp in (("fp16", 16), ("fp32", 16), ("fp16", 32)):
