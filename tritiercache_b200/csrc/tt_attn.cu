@@ -17,12 +17,17 @@
 //           scale folded into the weight (p*scale) and the zero into a
 //           running sum.
 //     Output: per (chunk, q head) partial (m, l, acc[hd]) and the raw logits
-//     (for the mean attention weights).
-//   k_attn_merge_heads grid = (q heads, jobs).  Log-sum-exp merge of a head's
-//     chunk partials into attn_output, and the head's (M, 1/L).
-//   k_attn_weights grid = (positions / 256, jobs).  The head-mean softmax
-//     weights (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed
-//     score feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
+//     (for the mean attention weights).  For engine steps the last CTA of
+//     each job merges the job's chunk partials (log-sum-exp) into attn_output
+//     and the heads' (M, 1/L) -- or, sequence-sharded, into the job's
+//     exchange row.
+//   k_attn_merge_heads grid = (q heads, jobs, groups).  The same merge for
+//     stand-alone calls and jobs with more than 128 chunk slots (two passes
+//     above 64 slots).
+//   k_attn_weights grid = (about 8 CTAs per SM over the launch, jobs), CTAs
+//     striding over positions.  The head-mean softmax weights
+//     (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed score
+//     feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
 #include <algorithm>
 
 #include "tt_attn.cuh"
