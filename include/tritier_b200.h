@@ -235,6 +235,7 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
  *   tt_engine_step_sharded_begin(..., xch_send)   maintenance + partial attention
  *       xch_send: n * num_q_heads * (head_dim + 2) floats (device)
  *   all-gather xch_send -> xch_all [world][n][num_q_heads][head_dim + 2]
+ *       (xch_all 8-byte aligned, else TT_ERR_INVALID_ARGUMENT)
  *   tt_engine_step_sharded_merge(..., xch_all, attn_output, mw_send)
  *       attn_output identical on every rank; mw_send: n * slot floats, this
  *       rank's mean attention weights

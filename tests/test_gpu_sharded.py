@@ -123,3 +123,10 @@ def test_sharded_step_argument_errors(C_):
     bad = C_.ShardedStep(eng, 2, 2)               # rank out of range
     with pytest.raises(ValueError):
         bad.begin(q, kv, kv, x, slot)
+    # the exchange rows are read as (m, l) pairs: an xch_all that is not
+    # 8-byte aligned is refused before any launch
+    xa = torch.zeros(2 * st.xch_floats + 1, device="cuda")
+    out = [torch.zeros(8 * 64, device="cuda")]
+    mw = torch.zeros(slot, device="cuda")
+    with pytest.raises(ValueError):
+        st.merge(xa[1:], out, mw, slot)

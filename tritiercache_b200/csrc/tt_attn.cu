@@ -261,19 +261,37 @@ __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ Attn
     float* IL = sm + nq;
     const size_t row = (size_t)HD + 2, rstride = (size_t)L.njobs * nq * row;
     const float* base = xch_all + (size_t)job * nq * row;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int h = warp; h < nq; h += NW) {
+    // (M, 1/L) of every head: 8 adjacent threads per head, each holding the
+    // (m, l) pairs of ranks sub, sub + 8, ... (one load round for P <= 8)
+    for (int h0 = 0; h0 < nq; h0 += NT / 8) {
+        const int h = h0 + threadIdx.x / 8, sub = threadIdx.x % 8;
+        constexpr int PR = 4;  // ranks per thread held in registers (P <= 32)
+        float2 ml[PR];
+#pragma unroll
+        for (int k = 0; k < PR; ++k) {
+            const int p = sub + 8 * k;
+            ml[k] = (h < nq && p < P) ? *reinterpret_cast<const float2*>(base + p * rstride + h * row)
+                                      : make_float2(-INFINITY, 0.f);
+        }
         float M = -INFINITY;
-        for (int p = lane; p < P; p += 32) M = fmaxf(M, base[p * rstride + h * row]);
-        M = warp_max(M);
+#pragma unroll
+        for (int k = 0; k < PR; ++k) M = fmaxf(M, ml[k].x);
+        for (int p = sub + 8 * PR; p < P && h < nq; p += 8) M = fmaxf(M, base[p * rstride + h * row]);
+#pragma unroll
+        for (int x = 1; x < 8; x <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
         float S = 0.f;
-        if (M != -INFINITY)
-            for (int p = lane; p < P; p += 32) {
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int k = 0; k < PR; ++k)
+                if (ml[k].x != -INFINITY) S = fmaf(ml[k].y, exp2f(ml[k].x - M), S);
+            for (int p = sub + 8 * PR; p < P && h < nq; p += 8) {
                 const float mp = base[p * rstride + h * row];
                 if (mp != -INFINITY) S = fmaf(base[p * rstride + h * row + 1], exp2f(mp - M), S);
             }
-        S = warp_sum(S);
-        if (lane == 0) {
+        }
+#pragma unroll
+        for (int x = 1; x < 8; x <<= 1) S += __shfl_xor_sync(0xffffffffu, S, x);
+        if (sub == 0 && h < nq) {
             Ms[h] = M;
             IL[h] = 1.0f / (S > 0.f ? S : 1.0f);
         }
@@ -301,15 +319,24 @@ __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ Attn
 }
 
 // Phase 3: every rank's mean weights -> score feedback for all positions.
-// grid (ceil(slot_cap / NT), njobs, world).
+// grid (ceil(slot_cap / (NT * kFeedbackPer)), njobs, world); each thread
+// updates kFeedbackPer positions (slots x*kFeedbackPer*NT + k*NT + thread),
+// with every load (weights, token ids, old scores) issued before its stores,
+// so a CTA pays the dependent-load chain once for several positions.
+constexpr int kFeedbackPer = 4;
 __global__ void __launch_bounds__(NT) k_shard_feedback(const __grid_constant__ AttnLaunch L, const float* mw_all,
                                                        int slot_cap) {
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y, p = blockIdx.z;
-    const int i = blockIdx.x * NT + threadIdx.x;
-    // the weight does not depend on the descriptor chain: load it first
-    const float w = i < slot_cap ? mw_all[((size_t)p * L.njobs + job) * slot_cap + i] : 0.f;
+    int idx[kFeedbackPer];
+    float w[kFeedbackPer];
+    const float* mwr = mw_all + ((size_t)p * L.njobs + job) * slot_cap;
+#pragma unroll
+    for (int k = 0; k < kFeedbackPer; ++k) {  // the weights do not depend on the descriptor chain
+        idx[k] = (blockIdx.x * kFeedbackPer + k) * NT + threadIdx.x;
+        w[k] = idx[k] < slot_cap ? mwr[idx[k]] : 0.f;
+    }
     if (threadIdx.x == 0) {
         Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
         Ts = resolve_counts(Js);
@@ -320,9 +347,25 @@ __global__ void __launch_bounds__(NT) k_shard_feedback(const __grid_constant__ A
     if (!J.g) return;
     const int D = tc.n0 + tc.n1 + tc.n2;
     const ShardRange R = shard_range(D, tc.nblk, J.grp, p, L.world);
-    const int n_loc = (R.dhi - R.dlo) + (R.phi - R.plo);
-    if (i >= n_loc || i >= slot_cap) return;
-    score_feedback(J, tc, D, shard_pos(R, D, i), w);
+    const int n_loc = min(slot_cap, (R.dhi - R.dlo) + (R.phi - R.plo));
+    long long id[kFeedbackPer];
+    int hh[kFeedbackPer];
+#pragma unroll
+    for (int k = 0; k < kFeedbackPer; ++k) {
+        hh[k] = -1;
+        id[k] = idx[k] < n_loc ? position_id(J, tc, D, shard_pos(R, D, idx[k]), hh[k]) : -1;
+        if (id[k] >= J.msl) id[k] = -1;
+    }
+    float g0[kFeedbackPer];
+#pragma unroll
+    for (int k = 0; k < kFeedbackPer; ++k) g0[k] = id[k] >= 0 ? J.g[id[k]] : 0.f;
+#pragma unroll
+    for (int k = 0; k < kFeedbackPer; ++k) {  // positions hold distinct tokens: no two updates meet
+        if (id[k] < 0) continue;
+        const float nv = fmaf(J.decay, g0[k], w[k]);
+        J.g[id[k]] = nv;
+        if (hh[k] >= 0) J.hh_scores[hh[k]] = nv;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -469,7 +512,7 @@ tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, float*
 }
 
 tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int slot_cap, cudaStream_t st) {
-    dim3 grid(std::max(1, ceil_div(slot_cap, NT)), L.njobs, L.world);
+    dim3 grid(std::max(1, ceil_div(slot_cap, NT * kFeedbackPer)), L.njobs, L.world);
     const int ps = prof_begin(2, st);
     k_shard_feedback<<<grid, NT, 0, st>>>(L, mw_all, slot_cap);
     prof_end(ps, st);

@@ -814,6 +814,7 @@ tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int ran
     tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
     if (s != TT_OK) return s;
     if (!xch_all || !attn_output || !mw_send) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if ((uintptr_t)xch_all & 7) return set_error(TT_ERR_INVALID_ARGUMENT, "xch_all must be 8-byte aligned.");
     for (int i = 0; i < n; ++i)
         if (!attn_output[i]) return set_error(TT_ERR_INVALID_ARGUMENT, "attn_output must not be NULL.");
     DeviceGuard dg(engines[0]->cfg.device);
