@@ -54,18 +54,6 @@ __device__ __forceinline__ long long position_id(const JobDesc& J, const TierCou
     return J.ids[pos - D];
 }
 
-// g[id] = decay * g[id] + w for the token at position pos, given its weight
-// (cache_engine.cpp:511-540); a heavy hitter's HH_scores copy follows; ids
-// outside [0, max_seq_len) are skipped.
-__device__ __forceinline__ void score_feedback(const JobDesc& J, const TierCounts& tc, int D, int pos, float w) {
-    int hh;
-    const long long id = position_id(J, tc, D, pos, hh);
-    if (id < 0 || id >= J.msl) return;
-    const float nv = fmaf(J.decay, J.g[id], w);
-    J.g[id] = nv;
-    if (hh >= 0) J.hh_scores[hh] = nv;
-}
-
 // The mean weight of position pos (written to mw when given) and, for
 // engines, g[id] = decay * g[id] + w for the token there (cache_engine.cpp:
 // 511-540): sinks, heavy hitters (whose HH_scores copy follows), the recent
