@@ -108,8 +108,13 @@ tt_status tt_fused_attention_decode(
  * on a device shares the one array and leaves its contents behind, so calls
  * that overlap on the GPU (different streams, or threads) race; keep them
  * ordered.  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.
- * Every GPU that loads the library holds the array until the process exits.
+ * (cudaGetSymbolAddress).  With CUDA's default lazy module loading that
+ * lookup is also what loads the module holding the array, so the first call
+ * on each device reserves the 32 MiB; make it at start-up, before reserving
+ * the device's memory and before any stream capture (or set
+ * CUDA_MODULE_LOADING=EAGER).  From then on the device holds the array until
+ * the process exits.  The address is cached per device for the life of the
+ * process; do not call this entry point again after a cudaDeviceReset.
  * No counterpart in the reference (its CPU kernel keeps thread-local scratch
  * vectors, fused_attn_avx2.cpp:139-143). */
 tt_status tt_fused_attention_decode_noalloc(

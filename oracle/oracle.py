@@ -26,8 +26,15 @@ def build(quiet: bool = True) -> None:
     """Compile liboracle.so (and the reference build when its sources exist)."""
     cmd = ["make", "-C", HERE]
     subprocess.run(cmd + (["-s"] if quiet else []), check=True)
-    if os.path.isdir(os.environ.get("REF_ROOT", "/root/reference") + "/csrc"):
-        subprocess.run(cmd + ["ref"] + (["-s"] if quiet else []), check=True)
+    ref = reference_root()
+    if os.path.isdir(os.path.join(ref, "csrc")):
+        subprocess.run(cmd + ["ref", f"REF_ROOT={ref}"] + (["-s"] if quiet else []), check=True)
+
+
+def reference_root() -> str:
+    """The reference checkout: $REF_ROOT, else a directory named `reference`
+    beside this repository's root (absent on machines that only run tests)."""
+    return os.environ.get("REF_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 
 def lib():
@@ -71,6 +78,7 @@ def _declare(L):
     L.orc_engine_buffer_bytes.restype = C.c_size_t
     L.orc_engine_buffer_bytes.argtypes = [vp]
     L.orc_engine_counters_get.argtypes = [vp, C.POINTER(EngineCounters)]
+    L.orc_engine_counters_set.argtypes = [vp, C.POINTER(EngineCounters)]
     L.orc_engine_buffer.restype = vp
     L.orc_engine_buffer.argtypes = [vp, i, C.POINTER(C.c_size_t), C.POINTER(C.c_int)]
     L.orc_f32_to_f16.restype = C.c_uint16
@@ -148,6 +156,14 @@ class Engine:
         c = EngineCounters()
         lib().orc_engine_counters_get(self.h, C.byref(c))
         return {n: getattr(c, n) for n, _ in EngineCounters._fields_}
+
+    def set_counters(self, **kw) -> None:
+        """Overwrite integer state (test set-up of synthetic tier layouts)."""
+        c = EngineCounters()
+        lib().orc_engine_counters_get(self.h, C.byref(c))
+        for k, v in kw.items():
+            setattr(c, k, v)
+        lib().orc_engine_counters_set(self.h, C.byref(c))
 
     def get_buffer_bytes(self):
         return lib().orc_engine_buffer_bytes(self.h)

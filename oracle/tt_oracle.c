@@ -710,6 +710,23 @@ void orc_engine_counters_get(const orc_engine* e, orc_engine_counters* c) {
     c->cached_threshold = e->cached_threshold;
 }
 
+/* Imports integer state built elsewhere (test infrastructure: synthetic tier
+ * layouts written through the buffers); pbs_allocated_blocks and the
+ * capacities are not touched. */
+void orc_engine_counters_set(orc_engine* e, const orc_engine_counters* c) {
+    e->s_count = c->s_count;
+    e->rw_count = c->rw_count;
+    e->rw_head = c->rw_head_index;
+    e->hh_count = c->hh_count;
+    e->wr_count = c->wr_count;
+    e->pbs_used = c->pbs_blocks_used;
+    e->pbs_count = c->pbs_count;
+    e->total = c->total_processed_tokens;
+    e->total_evictions = c->total_evictions;
+    e->last_calc_pos = c->last_calc_pos;
+    e->cached_threshold = c->cached_threshold;
+}
+
 void* orc_engine_buffer(orc_engine* e, int which, size_t* count, int* elem_size) {
     size_t kvs = e->kvs, nb = (size_t)e->pbs_alloc;
     int ms = e->p.meta_fp16 ? 2 : 4;

@@ -83,6 +83,8 @@ void orc_engine_prefill(orc_engine* e, const float* K_all, const float* V_all, i
 /* cache_engine.cpp:543-568 */
 size_t orc_engine_buffer_bytes(const orc_engine* e);
 void orc_engine_counters_get(const orc_engine* e, orc_engine_counters* c);
+/* test infrastructure: overwrite the integer state (not the capacities) */
+void orc_engine_counters_set(orc_engine* e, const orc_engine_counters* c);
 
 /* Raw buffer access (the reference exposes the same buffers as writable
  * zero-copy views, bindings.cpp:461-626).  which: 0 S_K, 1 S_V, 2 RW_K,

@@ -1,7 +1,8 @@
 """Generate the golden fixtures under tests/golden/ (run in the build container).
 
-Two sources, both from the reference project (path given by REF_ROOT,
-default /root/reference):
+Two sources, both from the reference project (its checkout is given by the
+REF_ROOT environment variable, or else is a directory named `reference` beside
+this repository's root):
 
 1. Known-answer vectors of the reference's own C++ tests, read as text:
    tests/test_quantize_v.cpp (16 tokens x 2 heads x head_dim 32 V block with
@@ -26,7 +27,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("REF_ROOT") or os.path.join(os.path.dirname(ROOT), "reference")
 
 
 def _cpp_array(src: str, name: str, kind: str):

@@ -9,8 +9,9 @@ views, as the reference exposes them (bindings.cpp:461-468, :537-544).  Then
 every counter, ring slot, heavy-hitter id/K/V, waiting-room id, packed word,
 metadata bit and PBS id must be bit-exact at every checked step; the GPU's
 own scores (before the sync) and the attention outputs are compared within
-tolerance.  An unsynchronised run reports the first step whose routing
-differs.
+tolerance (scores relative: |got - want| <= 1e-9 + 1e-4 |want|).  An
+unsynchronised run checks that membership stays the reference's (bounds in
+test_engine_unsynchronised_membership).
 """
 import numpy as np
 import pytest
@@ -102,7 +103,7 @@ def run_pair(C_, cfg, prefill, steps, seed, check_every=1, sync=True):
         assert ok, ("attention output", s, err)
         go = eo.buffer("global_attn_scores")
         gg = g_view.cpu().numpy()
-        ok, err = close(gg, go, atol=1e-5, rtol=1e-4)
+        ok, err = close(gg, go, atol=1e-9, rtol=1e-4)
         worst_g = max(worst_g, err)
         assert ok, ("scores", s, err)
         if sync:
@@ -138,32 +139,76 @@ def test_engine_config3_maintenance_run(C_):
     print(f"config-3 max |out err| {out_err:.3e}  max |score err| {g_err:.3e}")
 
 
-def test_engine_unsynchronised_divergence_report(C_):
-    """Without score sync the GPU engine routes on its own scores; report the
-    first step whose tier state differs from the oracle (informational)."""
-    cfg = (32, 8, 128, 8192, 4, 256, 0.05, 0.999, 32, 16, "fp16")
-    eo, eg = make_pair(C_, *cfg)
-    rng = np.random.default_rng(77)
-    P = 2048
-    Kp = rng.standard_normal((P, 8, 128)).astype(np.float32)
-    Vp = rng.standard_normal((P, 8, 128)).astype(np.float32)
-    eo.prefill(Kp, Vp, P)
-    eg.prefill(torch.from_numpy(Kp).cuda(), torch.from_numpy(Vp).cuda(), P)
+class _RefMembership:
+    """Tier membership of the reference's own engine (oracle/_ref), or of the
+    oracle port when that build is absent (the two are pinned bit-exact)."""
+
+    def __init__(self, cfg):
+        from oracle import oracle as O
+        R = O.load_reference()
+        self.ref = R is not None
+        self.e = R.TriTierCacheEngine(*cfg) if self.ref else O.Engine(*cfg)
+
+    def prefill(self, K, V, n):
+        self.e.prefill(K, V, n)
+
+    def step(self, q, k, v, out):
+        self.e.step(q, k, v, out)
+
+    def hh(self):
+        if self.ref:
+            return np.array(self.e.get_HH_token_ids())[: self.e.hh_count]
+        return self.e.buffer("HH_token_ids")[: self.e.counters()["hh_count"]].copy()
+
+    def pbs(self):
+        if self.ref:
+            return np.array(self.e.get_PBS_token_ids()).ravel()[: self.e.pbs_count]
+        return self.e.buffer("PBS_token_ids")[: self.e.counters()["pbs_count"]].copy()
+
+
+def test_engine_unsynchronised_membership(C_):
+    """Config 3 without score sync: the GPU engine routes on its own scores
+    (exp and sums in CUDA differ from AVX2/glibc in the last bits).  Over
+    prefill(4096) + 4096 decode steps the heavy-hitter set must agree exactly
+    for at least the first 256 steps, and at the end at least 95% of the heavy
+    hitters and 99% of the packed tokens must be the reference's."""
+    import bench
+    c = bench.CFG3
+    cfg = (c["nq"], c["nkv"], c["hd"], c["msl"], c["sink"], c["rw"], c["h_ratio"], c["decay"], c["ui"], c["grp"],
+           c["meta"])
+    ref = _RefMembership(cfg)
+    eg = C_.TriTierCacheEngine(*cfg)
+    Kp, Vp, X = bench.config3_inputs()
+    ref.prefill(Kp, Vp, c["prefill"])
+    eg.prefill(torch.from_numpy(Kp).cuda(), torch.from_numpy(Vp).cuda(), c["prefill"])
+    qn, kvs = c["nq"] * c["hd"], c["nkv"] * c["hd"]
+    Xd = torch.from_numpy(X).cuda()
+    og = torch.zeros(qn, device="cuda")
+    oo = np.zeros(qn, np.float32)
     first = None
-    for s in range(512):
-        Q = rng.standard_normal(32 * 128).astype(np.float32)
-        K = rng.standard_normal(8 * 128).astype(np.float32)
-        V = rng.standard_normal(8 * 128).astype(np.float32)
-        oo = np.zeros(32 * 128, np.float32)
-        eo.step(Q, K, V, oo)
-        og = torch.zeros(32 * 128, dtype=torch.float32, device="cuda")
-        eg.step(torch.from_numpy(Q).cuda(), torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(), og)
+    hh_g_view = eg.get_HH_token_ids()
+    for s in range(c["steps"]):
+        x = X[s]
+        ref.step(np.ascontiguousarray(x[:qn]), np.ascontiguousarray(x[qn:qn + kvs]),
+                 np.ascontiguousarray(x[qn + kvs:]), oo)
+        eg.step(Xd[s, :qn], Xd[s, qn:qn + kvs], Xd[s, qn + kvs:], og)
         if first is None:
-            ids_o = eo.buffer("HH_token_ids")
-            ids_g = gpu_state(eg, "HH_token_ids")
-            if not np.array_equal(ids_o, ids_g) or eo.counters()["hh_count"] != eg.counters()["hh_count"]:
+            hg = hh_g_view.cpu().numpy()
+            hr = ref.hh()
+            if not np.array_equal(np.sort(hg[hg >= 0]), np.sort(hr)):
                 first = s
-    print(f"unsynchronised run: first routing divergence at step {first} of 512")
+    hr, hg = ref.hh(), eg.get_HH_token_ids().cpu().numpy()
+    hg = hg[hg >= 0]
+    pr = ref.pbs()
+    pg = eg.get_PBS_token_ids().cpu().numpy()[: eg.counters()["pbs_count"]]
+    hh_agree = np.intersect1d(hr, hg).size / max(hr.size, 1)
+    pbs_agree = np.intersect1d(pr, pg).size / max(pr.size, 1)
+    print(f"unsynchronised config-3 run ({'reference build' if ref.ref else 'oracle port'}): first heavy-hitter "
+          f"divergence at step {first} of {c['steps']}; final agreement: heavy hitters {hh_agree:.4f} "
+          f"({hr.size} vs {hg.size}), packed tokens {pbs_agree:.4f} ({pr.size} vs {pg.size})")
+    assert first is None or first >= 256, first
+    assert hh_agree >= 0.95, hh_agree
+    assert pbs_agree >= 0.99, pbs_agree
 
 
 def test_engine_argument_errors(C_):

@@ -1,0 +1,213 @@
+"""GPU parity at the sizes of the benchmark configurations.
+
+The inputs come from bench.py's seeded synthetic workload (the same
+generator both benchmark arms use): per layer, K/V ~ N(0,1) with 4 outlier
+channels x8 (and RoPE for config 2), heavy hitters = the top 5% of the middle
+tokens by Exp(1) score, the rest 2-bit packed in id order.  The checker is
+the CPU oracle (itself pinned bit-exact to the reference's C++ kernels and
+engine by test_oracle_golden.py).
+
+Tolerances:
+* attention output: |got - want| <= 1e-4 + 1e-5 |want| (north-star FP32 bound);
+* mean attention weights and accumulated scores: |got - want| <=
+  1e-9 + 1e-4 |want| (relative: the weights average 1/T, so an absolute
+  bound of 1e-4 would accept anything at these lengths), and the weights
+  of every call sum to 1 within 1e-6;
+* packed words, metadata bits, ids, counters and tier membership: bit-exact.
+
+Configs (bench.CONFIGS / BASELINE configs): 1 = 32q/32kv MHA at 8k (fp16 and
+fp32 metadata), 2 = Llama-3-8B shape at 32k (1930 packed blocks), 5 = Qwen2-7B
+shape at 128k (28q/4kv, 7 query heads per kv head, 7766 packed blocks),
+4 = ragged batch of sequences with contexts in [2048, 65536] in one batched
+engine step.
+"""
+import numpy as np
+import pytest
+import torch
+
+import bench
+
+pytestmark = pytest.mark.gpu
+
+OUT_ATOL, OUT_RTOL = 1e-4, 1e-5
+W_ATOL, W_RTOL = 1e-9, 1e-4
+SUM_TOL = 1e-6
+
+
+@pytest.fixture(scope="module")
+def C_():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from tritiercache_b200 import _C
+    return _C
+
+
+@pytest.fixture(scope="module")
+def O_():
+    from oracle import oracle as O
+    return O
+
+
+def _within(got, want, atol, rtol):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    err = np.abs(got - want)
+    lim = atol + rtol * np.abs(want)
+    bad = np.nonzero(err > lim)[0]
+    return bad.size == 0, float(err.max()) if err.size else 0.0, bad[:5]
+
+
+def check_out(got, want, tag):
+    ok, err, bad = _within(got.ravel(), want.ravel(), OUT_ATOL, OUT_RTOL)
+    assert ok, (tag, "attention output", err, bad)
+
+
+def check_weights(got, want, tag):
+    ok, err, bad = _within(got, want, W_ATOL, W_RTOL)
+    assert ok, (tag, "mean weights", err, bad, got[bad], want[bad])
+    s = float(np.sum(np.asarray(got, np.float64)))
+    assert abs(s - 1.0) <= SUM_TOL, (tag, "sum of mean weights", s)
+
+
+def check_scores(got, want, tag):
+    ok, err, bad = _within(got, want, W_ATOL, W_RTOL)
+    assert ok, (tag, "scores", err, bad, got[bad], want[bad])
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def attention_case(C_, O_, cfg, layer, meta):
+    cfg = dict(cfg, meta=meta)
+    base = bench.base_kv(cfg, layer % bench.NBASE)
+    syn = bench.synth_layer(cfg, layer, base)
+    a = bench.ref_layer_arrays(bench._PortAdapter(O_), cfg, syn)
+    nq, nkv, hd, grp = cfg["nq"], cfg["nkv"], cfg["hd"], cfg["grp"]
+    q = bench.step_inputs(cfg)[0][layer, : nq * hd].reshape(nq, hd).copy()
+    T = a["dc"] + a["nb"] * grp
+    o_ref = np.zeros((nq, hd), np.float32)
+    mw_ref = np.zeros(T, np.float32)
+    O_.fused_attention_decode(q, a["dK"], a["dV"], a["dc"], a["kp"], a["ks"], a["kz"], a["vq"], a["vs"], a["vz"],
+                              a["ids"], a["nb"], nq, nkv, hd, o_ref, mw_ref, grp)
+    md = (lambda x: dev(x.view(np.int16))) if meta == "fp16" else dev
+    out = torch.zeros((nq, hd), device="cuda")
+    mw = torch.zeros(T, device="cuda")
+    C_.fused_attention_decode(dev(q), dev(a["dK"]), dev(a["dV"]), a["dc"], dev(a["kp"]), md(a["ks"]), md(a["kz"]),
+                              dev(a["vq"]), md(a["vs"]), md(a["vz"]), dev(a["ids"]), a["nb"], nq, nkv, hd, out, mw,
+                              grp, meta)
+    torch.cuda.synchronize()
+    tag = f"{cfg['key']} layer {layer} {meta}"
+    check_out(out.cpu().numpy(), o_ref, tag)
+    check_weights(mw.cpu().numpy(), mw_ref, tag)
+    return a
+
+
+@pytest.mark.parametrize("meta", ["fp16", "fp32"])
+def test_config1_attention_full_size(C_, O_, meta):
+    """32q/32kv MHA, 8k context: 657 dense tokens + 470 packed blocks."""
+    a = attention_case(C_, O_, bench.CONFIGS[1], 0, meta)
+    assert a["dc"] == 657 and a["nb"] == 470
+
+
+def test_config2_attention_full_size(C_, O_):
+    """One Llama-3-8B layer at 32k: 1886 dense tokens + 1930 packed blocks."""
+    a = attention_case(C_, O_, bench.CONFIGS[2], 0, "fp16")
+    assert a["dc"] == 1886 and a["nb"] == 1930
+
+
+def test_config5_attention_full_size(C_, O_):
+    """One Qwen2-7B layer at 128k: 28q/4kv (7 query heads per kv head), 6801
+    dense tokens + 7766 packed blocks."""
+    a = attention_case(C_, O_, bench.CONFIGS[5], 0, "fp16")
+    assert a["dc"] == 6801 and a["nb"] == 7766
+
+
+# ---------------------------------------------------------------------------
+# engines
+# ---------------------------------------------------------------------------
+STATE = ["S_K", "S_V", "RW_K", "RW_V", "HH_K", "HH_V", "HH_token_ids", "PBS_K_Packed", "PBS_K_Scales",
+         "PBS_K_Zeroes", "PBS_V_Packed", "PBS_V_Scales", "PBS_V_Zeroes", "PBS_token_ids", "WR_token_ids"]
+COUNTERS = ["s_count", "rw_count", "rw_head_index", "hh_count", "wr_count", "pbs_count", "pbs_blocks_used",
+            "total_processed_tokens", "total_evictions", "pbs_allocated_blocks", "last_calc_pos"]
+
+
+def compare_state(eo, eg, tag):
+    c, cg = eo.counters(), eg.counters()
+    for k in COUNTERS:
+        assert c[k] == cg[k], (tag, k, c[k], cg[k])
+    assert np.float32(c["cached_threshold"]).tobytes() == np.float32(cg["cached_threshold"]).tobytes(), tag
+    for n in STATE:
+        a = eo.buffer(n)
+        b = getattr(eg, "get_" + n)().cpu().numpy().ravel()
+        assert a.size == b.size, (tag, n, a.size, b.size)
+        assert np.array_equal(a.view(np.uint8), b.view(np.uint8)), (tag, n)
+
+
+def engine_pair(C_, O_, cfg, layer, base):
+    syn = bench.synth_layer(cfg, layer, base)
+    msl = cfg["ctx"] + 4096
+    eo = bench.oracle_engine(O_, cfg, syn, msl)
+    eg = bench.gpu_engine(C_, torch, cfg, syn, msl)
+    compare_state(eo, eg, f"{cfg['key']} import")
+    return eo, eg
+
+
+def sync_scores(eo, eg):
+    eg.get_global_attn_scores().copy_(dev(eo.buffer("global_attn_scores")))
+    eg.get_HH_scores().copy_(dev(eo.buffer("HH_scores")))
+
+
+def run_engine_steps(C_, O_, cfg, pairs, steps, seed):
+    """Steps every (oracle, GPU) pair with the same inputs; the GPU engines go
+    through ONE engine_step_batched call per step.  Score sync after each step."""
+    nq, nkv, hd = cfg["nq"], cfg["nkv"], cfg["hd"]
+    rng = np.random.default_rng(seed)
+    n = len(pairs)
+    for s in range(steps):
+        X = rng.standard_normal((n, nq * hd + 2 * nkv * hd), dtype=np.float32)
+        Xd = dev(X)
+        outs = torch.zeros((n, nq * hd), device="cuda")
+        C_.engine_step_batched([p[1] for p in pairs], Xd[:, : nq * hd], Xd[:, nq * hd: nq * hd + nkv * hd],
+                               Xd[:, nq * hd + nkv * hd:], outs)
+        og = outs.cpu().numpy()
+        for i, (eo, eg) in enumerate(pairs):
+            x = X[i]
+            oo = np.zeros(nq * hd, np.float32)
+            eo.step(x[: nq * hd].copy(), x[nq * hd: nq * hd + nkv * hd].copy(), x[nq * hd + nkv * hd:].copy(), oo)
+            tag = f"{cfg['key']} seq {i} step {s}"
+            check_out(og[i], oo, tag)
+            check_scores(eg.get_global_attn_scores().cpu().numpy(), eo.buffer("global_attn_scores"), tag)
+            sync_scores(eo, eg)
+            compare_state(eo, eg, tag)
+
+
+def test_config2_engine_steps_full_size(C_, O_):
+    """A Llama-3-8B layer's engine at 32k context (imported synthetic state),
+    four decode steps against the oracle engine."""
+    cfg = bench.CONFIGS[2]
+    base = bench.base_kv(cfg, 0)
+    run_engine_steps(C_, O_, cfg, [engine_pair(C_, O_, cfg, 0, base)], steps=4, seed=21)
+
+
+def test_config5_engine_steps_full_size(C_, O_):
+    """A Qwen2-7B layer's engine at 128k context, two decode steps."""
+    cfg = bench.CONFIGS[5]
+    base = bench.base_kv(cfg, 0)
+    run_engine_steps(C_, O_, cfg, [engine_pair(C_, O_, cfg, 0, base)], steps=2, seed=22)
+
+
+def test_config4_ragged_batch(C_, O_):
+    """Config 4: Mistral-7B shaped sequences (32q/8kv, hd 128) with seeded
+    contexts in [2048, 65536] stepped together by one engine_step_batched call
+    per step; every sequence is checked against its own oracle engine."""
+    rng = np.random.default_rng(4)
+    ctxs = sorted(int(c) for c in rng.integers(2048, 65537, 4))
+    ctxs[0], ctxs[-1] = 2048, 65536  # both ends of the range
+    big = dict(bench.CONFIGS[2], key="config4", ctx=max(ctxs), rope_theta=None)
+    base = bench.base_kv(big, 0)
+    pairs = []
+    for i, ctx in enumerate(ctxs):
+        cfg = dict(big, ctx=ctx)
+        pairs.append(engine_pair(C_, O_, cfg, i, (base[0][:ctx], base[1][:ctx])))
+    run_engine_steps(C_, O_, big, pairs, steps=3, seed=23)

@@ -347,6 +347,20 @@ class TriTierCacheEngine:
             check(lib().tt_engine_get_counters(self._h, C.byref(c)), "counters")
         return {n: getattr(c, n) for n, _ in _lib.EngineCounters._fields_}
 
+    def set_counters(self, **kw) -> None:
+        """Overwrite integer state (tt_engine_set_counters), stream-ordered on
+        the current stream: with the writable buffer views this imports a tier
+        layout built elsewhere.  Fields not given keep their current values.
+        No reference counterpart (its counters are read-only, bindings.cpp:437-458)."""
+        c = _lib.EngineCounters()
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_get_counters(self._h, C.byref(c)), "counters")
+            for k, v in kw.items():
+                if not hasattr(c, k):
+                    raise ValueError(f"unknown counter '{k}'")
+                setattr(c, k, v)
+            check(lib().tt_engine_set_counters(self._h, C.byref(c), _stream()), "set_counters")
+
     def _ctr(self, name):
         return self.counters()[name]
 
@@ -446,27 +460,43 @@ class TriTierCacheEngine:
         return self._view("PBS_token_ids", (self.pbs_allocated_blocks * self.chunk_size,))
 
 
+def _ptr_array(ts, n: int, name: str):
+    """ctypes array of n device pointers: `ts` is a sequence of contiguous
+    CUDA tensors, or one 2-D CUDA tensor whose n rows (each contiguous, any
+    row stride) are the entries (its pointers are computed without a Python
+    loop)."""
+    arr = C.c_void_p * n
+    if isinstance(ts, torch.Tensor):
+        if not (ts.is_cuda and ts.dim() == 2 and ts.shape[0] == n and (ts.stride(1) == 1 or ts.shape[1] == 1)):
+            raise ValueError(f"{name}: expected a 2-D CUDA tensor with {n} contiguous rows.")
+        row = ts.stride(0) * ts.element_size()
+        p = np.arange(n, dtype=np.uint64) * np.uint64(row) + np.uint64(ts.data_ptr())
+        return arr.from_buffer_copy(p.tobytes())
+    if len(ts) != n:
+        raise ValueError(f"{name}: expected {n} entries, got {len(ts)}.")
+    out = []
+    for t in ts:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous()):
+            raise ValueError(f"{name} entries must be contiguous CUDA tensors.")
+        out.append(t.data_ptr())
+    return arr(*out)
+
+
+def _handles(engines):
+    return (C.c_void_p * len(engines))(*[e._h.value for e in engines])
+
+
 def engine_step_batched(engines, Qs, Ks, Vs, outs) -> None:
     """One decode step for several engines (layers / sequences) in one set of
-    launches.  Every argument is a sequence of CUDA tensors (contiguous FP32);
-    no reference counterpart (the reference is batch-1, one engine per call)."""
+    launches.  Each of Qs / Ks / Vs / outs is a sequence of contiguous FP32
+    CUDA tensors, one per engine, or one contiguous tensor with a row per
+    engine.  No reference counterpart (the reference is batch-1, one engine
+    per call)."""
     n = len(engines)
-    if not (len(Qs) == len(Ks) == len(Vs) == len(outs) == n):
-        raise ValueError("engine_step_batched: argument lengths differ.")
-    arr = C.c_void_p * n
-    hs = arr(*[e._h.value for e in engines])
-
-    def ptrs(ts, name):
-        out = []
-        for t in ts:
-            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous()):
-                raise ValueError(f"engine_step_batched: {name} entries must be contiguous CUDA tensors.")
-            out.append(t.data_ptr())
-        return arr(*out)
-
     with torch.cuda.device(engines[0]._dev):
-        check(lib().tt_engine_step_batched(hs, n, ptrs(Qs, "Q"), ptrs(Ks, "K_new"), ptrs(Vs, "V_new"),
-                                           ptrs(outs, "attn_output"), _stream()), "engine_step_batched")
+        check(lib().tt_engine_step_batched(_handles(engines), n, _ptr_array(Qs, n, "Q"), _ptr_array(Ks, n, "K_new"),
+                                           _ptr_array(Vs, n, "V_new"), _ptr_array(outs, n, "attn_output"),
+                                           _stream()), "engine_step_batched")
 
 
 class ShardedStep:
@@ -480,73 +510,127 @@ class ShardedStep:
     def __init__(self, engines, rank: int, world: int):
         self.engines = list(engines)
         self.rank, self.world = int(rank), int(world)
-        n = len(self.engines)
-        self._arr = C.c_void_p * n
-        self._hs = self._arr(*[e._h.value for e in self.engines])
+        self.n = len(self.engines)
+        self._hs = _handles(self.engines)
         self.nq, self.hd = self.engines[0].num_q_heads, self.engines[0].head_dim
-        self.xch_floats = n * self.nq * (self.hd + 2)   # per rank
+        self.xch_floats = self.n * self.nq * (self.hd + 2)   # per rank
 
     def _ptrs(self, ts, name):
-        out = []
-        for t in ts:
-            if not (isinstance(t, torch.Tensor) and t.is_cuda and t.is_contiguous()):
-                raise ValueError(f"sharded step: {name} entries must be contiguous CUDA tensors.")
-            out.append(t.data_ptr())
-        return self._arr(*out)
+        return _ptr_array(ts, self.n, name)
 
     def slot_cap(self) -> int:
         """Mean-weight slots per engine this rank needs for the next step."""
         v = C.c_int()
-        check(lib().tt_engine_sharded_slot_cap(self._hs, len(self.engines), self.world, C.byref(v)), "slot_cap")
+        check(lib().tt_engine_sharded_slot_cap(self._hs, self.n, self.world, C.byref(v)), "slot_cap")
         return v.value
 
     def begin(self, Qs, Ks, Vs, xch_send: torch.Tensor, slot: int) -> None:
         with torch.cuda.device(self.engines[0]._dev):
-            check(lib().tt_engine_step_sharded_begin(self._hs, len(self.engines), self._ptrs(Qs, "Q"),
+            check(lib().tt_engine_step_sharded_begin(self._hs, self.n, self._ptrs(Qs, "Q"),
                                                      self._ptrs(Ks, "K_new"), self._ptrs(Vs, "V_new"), self.rank,
                                                      self.world, slot, xch_send.data_ptr(), _stream()), "begin")
 
     def merge(self, xch_all: torch.Tensor, outs, mw_send: torch.Tensor, slot: int) -> None:
         with torch.cuda.device(self.engines[0]._dev):
-            check(lib().tt_engine_step_sharded_merge(self._hs, len(self.engines), self.rank, self.world, slot,
+            check(lib().tt_engine_step_sharded_merge(self._hs, self.n, self.rank, self.world, slot,
                                                      xch_all.data_ptr(), self._ptrs(outs, "attn_output"),
                                                      mw_send.data_ptr(), _stream()), "merge")
 
     def end(self, mw_all: torch.Tensor, slot: int) -> None:
         with torch.cuda.device(self.engines[0]._dev):
-            check(lib().tt_engine_step_sharded_end(self._hs, len(self.engines), self.rank, self.world, slot,
+            check(lib().tt_engine_step_sharded_end(self._hs, self.n, self.rank, self.world, slot,
                                                    mw_all.data_ptr(), _stream()), "end")
 
 
-_shard_buffers: dict = {}
+class ShardedEngineStep:
+    """engine_step_batched over the ranks of a torch.distributed process group
+    (NCCL, one process per GPU), for one fixed list of engines: every rank
+    passes the same inputs and receives the same outputs; each attends 1/world
+    of the tokens.  The exchange buffers and the pointer arrays of the engines
+    are kept between calls.  With phase_timing(True) every call also records
+    CUDA events between its phases (device time per phase, phase_times())."""
+
+    PHASES = ("begin", "allgather_rows", "merge", "allgather_weights", "end")
+
+    def __init__(self, engines, rank=None, world=None, group=None):
+        import torch.distributed as dist
+        self.group = group
+        self.world = dist.get_world_size(group) if world is None else int(world)
+        self.rank = dist.get_rank(group) if rank is None else int(rank)
+        self.engines = list(engines)
+        self.step = ShardedStep(self.engines, self.rank, self.world)
+        self.dev = torch.device("cuda", self.engines[0]._dev)
+        self.buf = None
+        self._timing = False
+        self._acc = {p: 0.0 for p in self.PHASES}
+        self._pending = []
+
+    def _buffers(self, slot):
+        b = self.buf
+        if b is None or b["slot"] < slot:
+            s = max(slot, (b["slot"] * 5 // 4) if b else slot)
+            x = self.step.xch_floats
+            n = self.step.n
+            b = {"slot": s, "xs": torch.empty(x, device=self.dev), "xa": torch.empty(self.world * x, device=self.dev),
+                 "ms": torch.empty(n * s, device=self.dev), "ma": torch.empty(self.world * n * s, device=self.dev)}
+            self.buf = b
+        return b
+
+    def phase_timing(self, on: bool) -> None:
+        self._timing = bool(on)
+        self._acc = {p: 0.0 for p in self.PHASES}
+        self._pending = []
+
+    def phase_times(self, steps: int) -> dict:
+        """Device milliseconds per step of each phase over the timed calls."""
+        torch.cuda.synchronize(self.dev)
+        for ev in self._pending:
+            for p, a, b in zip(self.PHASES, ev[:-1], ev[1:]):
+                self._acc[p] += a.elapsed_time(b)
+        self._pending = []
+        return {p: round(v / max(steps, 1), 5) for p, v in self._acc.items()}
+
+    def __call__(self, engines, Qs, Ks, Vs, outs) -> None:
+        import torch.distributed as dist
+        if len(engines) != self.step.n or any(a is not b for a, b in zip(engines, self.engines)):
+            raise ValueError("ShardedEngineStep: called with a different list of engines.")
+        st = self.step
+        slot = st.slot_cap()
+        b = self._buffers(slot)
+        slot = b["slot"]
+        ev = None
+        if self._timing:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)]
+            ev[0].record()
+        st.begin(Qs, Ks, Vs, b["xs"], slot)
+        if ev:
+            ev[1].record()
+        dist.all_gather_into_tensor(b["xa"], b["xs"], group=self.group)
+        if ev:
+            ev[2].record()
+        st.merge(b["xa"], outs, b["ms"], slot)
+        if ev:
+            ev[3].record()
+        dist.all_gather_into_tensor(b["ma"], b["ms"], group=self.group)
+        if ev:
+            ev[4].record()
+        st.end(b["ma"], slot)
+        if ev:
+            ev[5].record()
+            self._pending.append(ev)
+
+
+_shard_steps: dict = {}
 
 
 def engine_step_batched_sharded(engines, Qs, Ks, Vs, outs, group=None) -> None:
     """engine_step_batched over the ranks of a torch.distributed process group
     (NCCL, one process per GPU): every rank passes the same engines' handles
     and the same inputs and receives the same outputs; each attends 1/world of
-    the tokens.  The exchange buffers are kept between calls."""
-    import torch.distributed as dist
-
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    n = len(engines)
-    if not (len(Qs) == len(Ks) == len(Vs) == len(outs) == n):
-        raise ValueError("engine_step_batched_sharded: argument lengths differ.")
-    step = ShardedStep(engines, rank, world)
-    slot = step.slot_cap()
-    dev = Qs[0].device
-    key = (dev, n, step.nq, step.hd, world)
-    buf = _shard_buffers.get(key)
-    if buf is None or buf["slot"] < slot:
-        slot_alloc = max(slot, (buf["slot"] * 5 // 4) if buf else slot)
-        buf = {"slot": slot_alloc,
-               "xs": torch.empty(step.xch_floats, device=dev), "xa": torch.empty(world * step.xch_floats, device=dev),
-               "ms": torch.empty(n * slot_alloc, device=dev), "ma": torch.empty(world * n * slot_alloc, device=dev)}
-        _shard_buffers[key] = buf
-    slot = buf["slot"]
-    step.begin(Qs, Ks, Vs, buf["xs"], slot)
-    dist.all_gather_into_tensor(buf["xa"], buf["xs"], group=group)
-    step.merge(buf["xa"], outs, buf["ms"], slot)
-    dist.all_gather_into_tensor(buf["ma"], buf["ms"], group=group)
-    step.end(buf["ma"], slot)
+    the tokens.  Keeps one ShardedEngineStep per (group, engine list)."""
+    key = (id(group), tuple(e._h.value for e in engines))
+    s = _shard_steps.get(key)
+    if s is None:
+        s = ShardedEngineStep(engines, group=group)
+        _shard_steps[key] = s
+    s(engines, Qs, Ks, Vs, outs)

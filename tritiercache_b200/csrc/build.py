@@ -8,6 +8,7 @@ quantize contract).
 """
 from __future__ import annotations
 
+import glob
 import os
 import subprocess
 import sys
@@ -15,8 +16,10 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 SOURCES = ["tt_api.cu", "tt_attn.cu", "tt_engine.cu", "tt_noalloc.cu"]
-HEADERS = ["tt_common.cuh", "tt_attn.cuh", "tt_partial.cuh", "tt_pbs_mma.cuh",
-           os.path.join("..", "..", "include", "tritier_b200.h")]
+# every header in this directory (and the C ABI header) is a dependency of
+# every object: editing any of them rebuilds all sources
+HEADERS = sorted(os.path.basename(h) for h in glob.glob(os.path.join(HERE, "*.cuh"))) + \
+    [os.path.join("..", "..", "include", "tritier_b200.h")]
 LIB = os.path.join(PKG, "libtritier_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",

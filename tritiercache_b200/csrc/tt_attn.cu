@@ -29,6 +29,8 @@
 //     (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed score
 //     feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
 #include <algorithm>
+#include <climits>
+#include <mutex>
 
 #include "tt_attn.cuh"
 
@@ -422,17 +424,19 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
 template <int HD, int GM, bool MMA>
 static tt_status launch_partial_t(const AttnLaunch& L, cudaStream_t st) {
     const size_t sm = kernel_smem_bytes<HD, GM, MMA>(L.HG, L.meta_bytes);
-    static bool configured[64] = {};
+    // the shared-memory limit is a per-device function attribute: set it once
+    // per device, also when several host threads launch at the same time
+    static std::once_flag once[64];
+    static cudaError_t once_err[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!configured[dev & 63]) {
+    std::call_once(once[dev & 63], [&] {
         size_t mx = 0;
         for (int hg = 1; hg <= 8; ++hg) mx = std::max(mx, kernel_smem_bytes<HD, GM, MMA>(hg, 4));
-        cudaError_t e = cudaFuncSetAttribute(k_attn_partial<HD, GM, MMA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)mx);
-        if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(k_attn_partial)");
-        configured[dev & 63] = true;
-    }
+        once_err[dev & 63] = cudaFuncSetAttribute(k_attn_partial<HD, GM, MMA>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
+    });
+    if (once_err[dev & 63] != cudaSuccess) return check_cuda(once_err[dev & 63], "cudaFuncSetAttribute(k_attn_partial)");
     dim3 grid(L.nd + L.np, L.njobs * L.nhg);
     const int ps = prof_begin(1, st);
     k_attn_partial<HD, GM, MMA><<<grid, NT, sm, st>>>(L);
@@ -635,7 +639,10 @@ extern "C" tt_status tt_fused_attention_decode(const float* Q, const float* dens
     AttnLaunch L;
     memset(&L, 0, sizeof(L));
     L.njobs = 1;
-    const int ntok = num_blocks * k_group_size;
+    const long long ntok_ll = (long long)num_blocks * k_group_size;
+    if (ntok_ll + dense_count > INT_MAX)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "num_blocks * k_group_size + dense_count exceeds INT_MAX.");
+    const int ntok = (int)ntok_ll;
     tt_status s = plan_attention(L, num_q_heads, num_kv_heads, head_dim, dense_count, ntok);
     if (s != TT_OK) return s;
     int dev = 0;

@@ -10,9 +10,15 @@
 // is not allowed.  For them this file provides one more entry point whose
 // scratch is a fixed array in device memory, declared at file scope.
 //
-// The array costs kNoAllocScratchBytes of device memory on every GPU that
-// loads the library, from module load until process exit, whether or not the
-// entry point is used.
+// The array costs kNoAllocScratchBytes of device memory on every GPU where
+// the module that holds it is loaded, until the process exits.  CUDA 12 loads
+// modules lazily by default, so that happens at the first call of this entry
+// point on each device (its cudaGetSymbolAddress is the first use of the
+// module): the 32 MiB are reserved then, not when the library is opened.
+// Callers that reserve device memory up front make one call at start-up,
+// before they reserve and before any stream capture (or run with
+// CUDA_MODULE_LOADING=EAGER, which loads it with the library).
+#include <climits>
 #include <mutex>
 
 #include "tt_attn.cuh"
@@ -24,6 +30,10 @@ constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;  // 32 MiB
 // Only device code may name this array directly.  In host code its name is a
 // host-side stand-in, not a device address, so host code obtains the address
 // with cudaGetSymbolAddress (once per device, with that device current).
+// That lookup is also what makes a lazily loading runtime load this module
+// and reserve the array on the device.  The address is cached per device for
+// the life of the process: after a cudaDeviceReset the cached value is stale
+// and this entry point must not be called again in that process.
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_mu;
@@ -76,7 +86,10 @@ extern "C" tt_status tt_fused_attention_decode_noalloc(
     AttnLaunch L;
     memset(&L, 0, sizeof(L));
     L.njobs = 1;
-    const int ntok = num_blocks * k_group_size;
+    const long long ntok_ll = (long long)num_blocks * k_group_size;
+    if (ntok_ll + dense_count > INT_MAX)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "num_blocks * k_group_size + dense_count exceeds INT_MAX.");
+    const int ntok = (int)ntok_ll;
     tt_status s = plan_attention(L, num_q_heads, num_kv_heads, head_dim, dense_count, ntok);
     if (s != TT_OK) return s;
 
