@@ -266,6 +266,37 @@ tt_status tt_engine_step_sharded_end(tt_engine* const* engines, int n, int rank,
 tt_status tt_engine_prefill(tt_engine* e, const float* K_all, const float* V_all, int q_len,
                             void* stream);
 
+/* The per-token half of the reference's full-weights decode path
+ * (output_attentions=True, src/tri_tier/integration/patch_model.py:163-169):
+ *
+ * tt_engine_ingest replaces TriTierCache.ingest_token (src/tri_tier/cache.py:
+ * 206-233): the new token K_new/V_new [num_kv_heads*head_dim] enters the sink
+ * / ring tiers and the evicted ring token is routed and, with a full waiting
+ * room, quantized -- the engine's own maintenance (cache_engine.cpp:405-431,
+ * :209-269), without attention and without score feedback.  Stream-ordered. */
+tt_status tt_engine_ingest(tt_engine* e, const float* K_new, const float* V_new, void* stream);
+
+/* Number of positions tt_engine_reconstruct returns: sinks + heavy hitters +
+ * live packed tokens + ring.  Synchronises. */
+tt_status tt_engine_full_count(tt_engine* e, int* count);
+
+/* Replaces TriTierCache.reconstruct_full_cache (src/tri_tier/cache.py:326-372):
+ * K_out/V_out [capacity, num_kv_heads, head_dim] float32 and ids_out
+ * [capacity] int64 receive the rows [sinks | heavy hitters and live packed
+ * tokens in token-id order | ring in logical order], packed tokens
+ * dequantized as code*scale + zero (two roundings, as the reference's torch
+ * expression).  *count = rows written; capacity below it ->
+ * TT_ERR_INVALID_ARGUMENT (nothing written).  Synchronises. */
+tt_status tt_engine_reconstruct(tt_engine* e, float* K_out, float* V_out, int64_t* ids_out, int capacity,
+                                int* count, void* stream);
+
+/* Replaces TriTierCache.accumulate_attn_scrs (src/tri_tier/cache.py:164-187):
+ * global_attn_scores[ids[i]] += mean over heads of weights[h][i] for every
+ * i < n with ids[i] in [0, max_seq_len) (undecayed; ids NULL means ids[i] = i).
+ * weights [n_heads, n] float32.  Stream-ordered. */
+tt_status tt_engine_accumulate_scores(tt_engine* e, const float* weights, const int64_t* ids, int n_heads, int n,
+                                      void* stream);
+
 /* Reads the device-side counters (synchronises the engine's last stream). */
 tt_status tt_engine_get_counters(tt_engine* e, tt_engine_counters* out);
 

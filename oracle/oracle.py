@@ -184,6 +184,65 @@ class Engine:
         return np.frombuffer(arr, dtype=dt, count=n.value)
 
 
+def _meta_f32(a, meta16):
+    a = np.asarray(a)
+    return a.view(np.float16).astype(np.float32) if meta16 else a.astype(np.float32)
+
+
+def reconstruct_full_cache(st: dict):
+    """src/tri_tier/cache.py:326-372 restated in numpy over an engine state
+    dump `st` (tier buffers in the engine layouts plus the counters):
+    [sinks | heavy hitters and live packed tokens sorted by id | ring in
+    logical order]; packed tokens dequantized as code * scale + zero with two
+    float32 roundings (the reference's torch expression).  Group 16 or 32."""
+    S, hh, rw, head = st["s_count"], st["hh_count"], st["rw_count"], st["rw_head_index"]
+    R, grp, nkv, hd, m16 = st["rw_size"], st["grp"], st["nkv"], st["hd"], st["meta16"]
+    total, nb = st["total"], st["pbs_blocks_used"]
+    kvs = nkv * hd
+    sK = st["S_K"].reshape(-1, nkv, hd)[:S]
+    sV = st["S_V"].reshape(-1, nkv, hd)[:S]
+    sid = np.arange(S, dtype=np.int64)
+    n = nb * grp
+    kp = st["PBS_K_Packed"].reshape(-1, kvs)[: nb * (grp // 16)].view(np.uint32).reshape(nb, grp // 16, nkv, hd)
+    t = np.arange(grp)
+    codes = (kp[:, t // 16, :, :] >> (2 * (t % 16)).astype(np.uint32)[None, :, None, None]) & 3  # [nb][grp][nkv][hd]
+    ks = _meta_f32(st["PBS_K_Scales"], m16).reshape(-1, nkv, hd)[:nb]
+    kz = _meta_f32(st["PBS_K_Zeroes"], m16).reshape(-1, nkv, hd)[:nb]
+    pK = (codes.astype(np.float32) * ks[:, None]) + kz[:, None]
+    pK = pK.reshape(n, nkv, hd)
+    qhd = (hd + 15) // 16
+    vp = st["PBS_V_Packed"].reshape(-1, nkv, qhd)[:n].view(np.uint32)
+    c = np.arange(hd)
+    vcodes = (vp[:, :, c // 16] >> (2 * (c % 16)).astype(np.uint32)[None, None, :]) & 3  # [n][nkv][hd]
+    vs = _meta_f32(st["PBS_V_Scales"], m16).reshape(-1, nkv)[:n]
+    vz = _meta_f32(st["PBS_V_Zeroes"], m16).reshape(-1, nkv)[:n]
+    pV = (vcodes.astype(np.float32) * vs[:, :, None]) + vz[:, :, None]
+    pid = st["PBS_token_ids"][:n]
+    live = pid != -1
+    mK = np.concatenate([st["HH_K"].reshape(-1, nkv, hd)[:hh], pK[live]])
+    mV = np.concatenate([st["HH_V"].reshape(-1, nkv, hd)[:hh], pV[live]])
+    mid = np.concatenate([st["HH_token_ids"][:hh], pid[live]])
+    perm = np.argsort(mid, kind="stable")
+    mK, mV, mid = mK[perm], mV[perm], mid[perm]
+    rK = st["RW_K"].reshape(-1, nkv, hd)
+    rV = st["RW_V"].reshape(-1, nkv, hd)
+    if rw < R:
+        rK, rV = rK[:rw], rV[:rw]
+        rid = np.arange(S, S + rw, dtype=np.int64)
+    else:
+        rK, rV = np.roll(rK, -head, axis=0), np.roll(rV, -head, axis=0)
+        rid = np.arange(total - R, total, dtype=np.int64)
+    return (np.concatenate([sK, mK, rK]).astype(np.float32), np.concatenate([sV, mV, rV]).astype(np.float32),
+            np.concatenate([sid, mid, rid]).astype(np.int64))
+
+
+def accumulate_attn_scrs(g, weights, ids):
+    """src/tri_tier/cache.py:164-187: g[ids] += weights.mean(heads), skipping -1."""
+    mean = np.asarray(weights, np.float32).mean(axis=0, dtype=np.float32)
+    ok = ids != -1
+    np.add.at(g, ids[ok], mean[ok])
+
+
 def load_reference():
     """The reference `_C` compiled from its own sources into oracle/_ref/, or None."""
     cands = glob.glob(os.path.join(HERE, "_ref", "_C*.so"))

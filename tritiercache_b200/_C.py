@@ -459,6 +459,52 @@ class TriTierCacheEngine:
     def get_PBS_token_ids(self):
         return self._view("PBS_token_ids", (self.pbs_allocated_blocks * self.chunk_size,))
 
+    # -- full-weights path (output_attentions) ----------------------------------
+    def ingest(self, k_ptr, v_ptr) -> None:
+        """Maintenance only: ingest one token and route the evicted one, no
+        attention, no score feedback (tt_engine_ingest)."""
+        kvs = self.num_kv_heads * self.head_dim
+        k = _arg(k_ptr, "K_new", kvs * 4)
+        v = _arg(v_ptr, "V_new", kvs * 4)
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_ingest(self._h, k.ptr, v.ptr, _stream()), "ingest")
+        self._keep = (k, v)
+
+    def reconstruct(self):
+        """(K_full, V_full, ids) CUDA tensors of the whole cache in token-id
+        order with the packed tier dequantized (tt_engine_reconstruct)."""
+        n = C.c_int()
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_full_count(self._h, C.byref(n)), "reconstruct")
+            cap = max(n.value, 1)
+            K = torch.empty((cap, self.num_kv_heads, self.head_dim), device=self.device)
+            V = torch.empty((cap, self.num_kv_heads, self.head_dim), device=self.device)
+            ids = torch.empty(cap, dtype=torch.int64, device=self.device)
+            got = C.c_int()
+            check(lib().tt_engine_reconstruct(self._h, K.data_ptr(), V.data_ptr(), ids.data_ptr(), cap,
+                                              C.byref(got), _stream()), "reconstruct")
+        m = got.value
+        return K[:m], V[:m], ids[:m]
+
+    def accumulate_scores(self, weights: torch.Tensor, ids: Optional[torch.Tensor] = None) -> None:
+        """global_attn_scores[ids] += weights.mean(0) (undecayed,
+        tt_engine_accumulate_scores); weights [heads, n], ids [n] int64 or None."""
+        w = weights.to(device=self.device, dtype=torch.float32).contiguous()
+        if w.dim() != 2:
+            raise ValueError("weights must be [heads, n].")
+        n = w.shape[1]
+        idp = None
+        idt = None
+        if ids is not None:
+            idt = ids.to(device=self.device, dtype=torch.int64).contiguous()
+            if idt.numel() != n:
+                raise ValueError("ids must have one entry per position.")
+            idp = idt.data_ptr()
+        with torch.cuda.device(self._dev):
+            check(lib().tt_engine_accumulate_scores(self._h, w.data_ptr(), idp, w.shape[0], n, _stream()),
+                  "accumulate_scores")
+        self._keep = (w, idt)
+
 
 def _ptr_array(ts, n: int, name: str):
     """ctypes array of n device pointers: `ts` is a sequence of contiguous

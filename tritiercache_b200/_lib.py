@@ -63,6 +63,7 @@ EXPORTS = [
     "tt_engine_device_bytes", "tt_engine_set_counters", "tt_profile_enable", "tt_profile_collect",
     "tt_device_error", "tt_fused_attention_decode_noalloc", "tt_engine_sharded_slot_cap",
     "tt_engine_step_sharded_begin", "tt_engine_step_sharded_merge", "tt_engine_step_sharded_end",
+    "tt_engine_ingest", "tt_engine_full_count", "tt_engine_reconstruct", "tt_engine_accumulate_scores",
 ]
 
 _lib = None
@@ -103,6 +104,10 @@ def _declare(L):
     L.tt_engine_step_sharded_begin.argtypes = [pv, i, pv, pv, pv, i, i, i, vp, vp]
     L.tt_engine_step_sharded_merge.argtypes = [pv, i, i, i, i, vp, pv, vp, vp]
     L.tt_engine_step_sharded_end.argtypes = [pv, i, i, i, i, vp, vp]
+    L.tt_engine_ingest.argtypes = [vp, vp, vp, vp]
+    L.tt_engine_full_count.argtypes = [vp, C.POINTER(i)]
+    L.tt_engine_reconstruct.argtypes = [vp, vp, vp, vp, i, C.POINTER(i), vp]
+    L.tt_engine_accumulate_scores.argtypes = [vp, vp, vp, i, i, vp]
     for name in EXPORTS:
         if name not in ("tt_last_error", "tt_version"):
             getattr(L, name).restype = C.c_int

@@ -84,6 +84,43 @@ class TriTierCache:
         """The reference engine's byte formula (cache_engine.cpp:543-568)."""
         return self._engine.get_buffer_bytes()
 
+    # -- full-weights path (output_attentions=True, patch_model.py:163-169) ----
+    def ingest_token(self, K: torch.Tensor, V: torch.Tensor) -> None:
+        """Ingests one token [num_heads, head_dim] and routes the evicted one
+        (cache.py:206-233).  Routing and quantization are the engine's
+        (cache_engine.cpp:209-269: cached percentile threshold, strict-min
+        demotion, 16-token waiting room); the reference's pure-torch fallback
+        routes with torch.quantile instead, a different rule."""
+        Kd = K.to(device=self.device, dtype=torch.float32).contiguous()
+        Vd = V.to(device=self.device, dtype=torch.float32).contiguous()
+        self._engine.ingest(Kd, Vd)
+
+    def reconstruct_full_cache(self):
+        """(K_full, V_full, full_ids): sinks, heavy hitters and packed tokens in
+        token-id order (packed ones dequantized), then the ring in logical
+        order (cache.py:326-372); CUDA tensors."""
+        return self._engine.reconstruct()
+
+    def accumulate_attn_scrs(self, attn_weights: torch.Tensor, full_ids=None) -> None:
+        """Adds the head-mean of one decode step's attention weights to the
+        accumulated scores, undecayed (cache.py:164-187)."""
+        if attn_weights.dim() == 4:
+            if attn_weights.shape[2] > 1:
+                raise RuntimeError("Multi-token prefill not supported in single-step accumulate")
+            step = attn_weights.squeeze(0).squeeze(1)
+        elif attn_weights.dim() == 3:
+            step = attn_weights.squeeze(1)
+        else:
+            step = attn_weights
+        if step.dim() == 1:
+            step = step.unsqueeze(0)
+        self._engine.accumulate_scores(step, full_ids)
+
+    def fetch_or_calc_thresh(self, total_processed_tokens: int = 0):
+        """The engine's cached heavy-hitter threshold (cache_engine.cpp:118-146),
+        as a tensor (cache.py:189-204 returns its own quantile)."""
+        return torch.tensor(float(self._engine.counters()["cached_threshold"]))
+
     def assert_evictions_occurred(self) -> None:
         """cache.py:156-162."""
         assert self.total_evictions > 0 or self.PBS_count > 0 or self.HH_count > 0, (

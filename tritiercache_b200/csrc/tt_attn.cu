@@ -5,22 +5,22 @@
 // background store (PBS) into scratch, materialises an nq x T score matrix
 // and walks it per query head.  Here the work is split-KV:
 //
-//   k_attn_partial  grid = (token chunks, jobs x kv-head groups), 8 warps.
-//     Each warp owns one kv head and walks 32-token units of its chunk:
-//       QK  Dense rows: FP32 dot with the G query heads of the kv head (GQA:
-//           every K byte is read once).  Packed rows: 2-bit codes used in
-//           place as 4 + code (tensor-core unit, tt_pbs_mma.cuh, or the SIMT
-//           unit): score = sum(q*scale*(4+code)) - 4 sum(q*scale) + sum(q*zero),
-//           no dequantized copy.
-//       online softmax in log2 units (exp2).
-//       PV  Dense V rows read coalesced; packed V codes with the per-token
-//           scale folded into the weight (p*scale) and the zero into a
-//           running sum.
-//     Output: per (chunk, q head) partial (m, l, acc[hd]) and the raw logits
-//     (for the mean attention weights).  For engine steps the last CTA of
-//     each job merges the job's chunk partials (log-sum-exp) into attn_output
-//     and the heads' (M, 1/L) -- or, sequence-sharded, into the job's
-//     exchange row.
+//   k_attn_dense   grid = (dense chunks, jobs x kv-head groups), 8 warps
+//     (tt_dense.cuh).  The FP32 sink / heavy-hitter / ring rows staged by 1-D
+//     TMA bulk copies: QK with the G query heads of each kv head (GQA: every
+//     K byte is read once), online softmax in log2 units, PV.
+//   k_attn_packed  grid = (packed chunks, jobs x kv-head groups), 8 warps
+//     (tt_partial.cuh).  2-bit codes used in place as 4 + code (tensor-core
+//     unit, tt_pbs_mma.cuh, or the SIMT unit): score = sum(q*scale*(4+code))
+//     - 4 sum(q*scale) + sum(q*zero), no dequantized copy; the per-token V
+//     scale folded into the weight, the zero into a running sum.
+//   The two run concurrently (the dense one on a second stream, forked and
+//   joined with events): the memory-bound dense chunks and the issue-bound
+//   packed chunks share the SMs.  Output: per (chunk, q head) partial
+//   (m, l, acc[hd]) and the raw logits (for the mean attention weights).
+//   For engine steps the last CTA of each job, of either kernel, merges the
+//   job's chunk partials (log-sum-exp) into attn_output and the heads'
+//   (M, 1/L) -- or, sequence-sharded, into the job's exchange row.
 //   k_attn_merge_heads grid = (q heads, jobs, groups).  The same merge for
 //     stand-alone calls and jobs with more than 128 chunk slots (two passes
 //     above 64 slots).
@@ -35,6 +35,7 @@
 #include "tt_attn.cuh"
 
 #include "tt_partial.cuh"
+#include "tt_dense.cuh"
 
 namespace tt {
 
@@ -421,63 +422,117 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
     return TT_OK;
 }
 
-template <int HD, int GM, bool MMA>
-static tt_status launch_partial_t(const AttnLaunch& L, cudaStream_t st) {
-    const size_t sm = kernel_smem_bytes<HD, GM, MMA>(L.HG, L.meta_bytes);
-    // the shared-memory limit is a per-device function attribute: set it once
-    // per device, also when several host threads launch at the same time
+// Sets a kernel's dynamic shared-memory limit once per device (a per-device
+// function attribute), also when several host threads launch at once; one
+// flag set per kernel instantiation.
+template <auto Kernel>
+static tt_status smem_limit_once(size_t bytes, const char* what) {
     static std::once_flag once[64];
-    static cudaError_t once_err[64];
+    static cudaError_t err[64];
     int dev = 0;
     cudaGetDevice(&dev);
     std::call_once(once[dev & 63], [&] {
-        size_t mx = 0;
-        for (int hg = 1; hg <= 8; ++hg) mx = std::max(mx, kernel_smem_bytes<HD, GM, MMA>(hg, 4));
-        once_err[dev & 63] = cudaFuncSetAttribute(k_attn_partial<HD, GM, MMA>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx);
+        err[dev & 63] = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
     });
-    if (once_err[dev & 63] != cudaSuccess) return check_cuda(once_err[dev & 63], "cudaFuncSetAttribute(k_attn_partial)");
-    dim3 grid(L.nd + L.np, L.njobs * L.nhg);
-    const int ps = prof_begin(1, st);
-    k_attn_partial<HD, GM, MMA><<<grid, NT, sm, st>>>(L);
-    prof_end(ps, st);
-    return check_launch("k_attn_partial");
+    return err[dev & 63] == cudaSuccess ? TT_OK : check_cuda(err[dev & 63], what);
+}
+
+template <int HD, int GM, bool MMA>
+static tt_status launch_packed_t(const AttnLaunch& L, cudaStream_t st) {
+    size_t mx = 0;
+    for (int hg = 1; hg <= 8; ++hg) mx = std::max(mx, kernel_smem_bytes<HD, GM, MMA>(hg, 4));
+    tt_status s = smem_limit_once<k_attn_packed<HD, GM, MMA>>(mx, "cudaFuncSetAttribute(k_attn_packed)");
+    if (s != TT_OK) return s;
+    k_attn_packed<HD, GM, MMA><<<dim3(L.np, L.njobs * L.nhg), NT, kernel_smem_bytes<HD, GM, MMA>(L.HG, L.meta_bytes), st>>>(L);
+    return check_launch("k_attn_packed");
+}
+
+template <int HD, int GM>
+static tt_status launch_dense_t(const AttnLaunch& L, cudaStream_t st) {
+    size_t mx = 0;
+    for (int hg = 1; hg <= 8; ++hg) mx = std::max(mx, dense_smem_bytes<HD, GM>(hg));
+    tt_status s = smem_limit_once<k_attn_dense<HD, GM>>(mx, "cudaFuncSetAttribute(k_attn_dense)");
+    if (s != TT_OK) return s;
+    k_attn_dense<HD, GM><<<dim3(L.nd, L.njobs * L.nhg), NT, dense_smem_bytes<HD, GM>(L.HG), st>>>(L);
+    return check_launch("k_attn_dense");
 }
 
 // Packed chunks run on the tensor cores (mma.sync f16) for head_dim 64 / 128,
 // up to 4 query heads per kv head, an even number of kv heads and fp16
 // metadata in every job of the batch; other shapes keep the SIMT unit.
 template <int HD, int GM>
-static tt_status launch_partial_g(const AttnLaunch& L, cudaStream_t st) {
+static tt_status launch_packed_g(const AttnLaunch& L, cudaStream_t st) {
     if constexpr ((HD == 64 || HD == 128) && GM <= 4) {
-        if (L.meta_bytes == 2 && (L.HG * L.nhg) % 2 == 0) return launch_partial_t<HD, GM, true>(L, st);
+        if (L.meta_bytes == 2 && (L.HG * L.nhg) % 2 == 0) return launch_packed_t<HD, GM, true>(L, st);
     }
-    return launch_partial_t<HD, GM, false>(L, st);
+    return launch_packed_t<HD, GM, false>(L, st);
 }
 
+// which: 0 dense kernel, 1 packed kernel
 template <int HD>
-static tt_status launch_partial_hd(const AttnLaunch& L, cudaStream_t st) {
+static tt_status launch_kind_hd(const AttnLaunch& L, int which, cudaStream_t st) {
     switch (pick_gm(L.G)) {
-        case 1: return launch_partial_g<HD, 1>(L, st);
-        case 2: return launch_partial_g<HD, 2>(L, st);
-        case 4: return launch_partial_g<HD, 4>(L, st);
+        case 1: return which ? launch_packed_g<HD, 1>(L, st) : launch_dense_t<HD, 1>(L, st);
+        case 2: return which ? launch_packed_g<HD, 2>(L, st) : launch_dense_t<HD, 2>(L, st);
+        case 4: return which ? launch_packed_g<HD, 4>(L, st) : launch_dense_t<HD, 4>(L, st);
         case 8:
-            if constexpr (HD <= 128) return launch_partial_g<HD, 8>(L, st);
+            if constexpr (HD <= 128) return which ? launch_packed_g<HD, 8>(L, st) : launch_dense_t<HD, 8>(L, st);
             return set_error(TT_ERR_UNSUPPORTED, "head_dim 256 supports at most 4 query heads per kv head");
     }
     return set_error(TT_ERR_UNSUPPORTED, "unsupported GQA ratio");
 }
 
-static tt_status launch_partial_any(const AttnLaunch& L, cudaStream_t st) {
-    if (L.nd + L.np == 0) return TT_OK;
+static tt_status launch_kind(const AttnLaunch& L, int which, cudaStream_t st) {
     switch (L.inline_job.hd) {  // callers always fill inline_job.hd/nq (also for engine batches)
-        case 16: return launch_partial_hd<16>(L, st);
-        case 32: return launch_partial_hd<32>(L, st);
-        case 64: return launch_partial_hd<64>(L, st);
-        case 128: return launch_partial_hd<128>(L, st);
-        case 256: return launch_partial_hd<256>(L, st);
+        case 16: return launch_kind_hd<16>(L, which, st);
+        case 32: return launch_kind_hd<32>(L, which, st);
+        case 64: return launch_kind_hd<64>(L, which, st);
+        case 128: return launch_kind_hd<128>(L, which, st);
+        case 256: return launch_kind_hd<256>(L, which, st);
         default: return set_error(TT_ERR_UNSUPPORTED, "unsupported head_dim");
     }
+}
+
+// A second stream per device for the dense kernel, forked from and joined
+// back into the caller's stream with events, so that the dense (memory-bound)
+// and packed (issue-bound) chunks share the GPU.  Stream capture follows the
+// fork into the side stream and back.
+struct SideStream {
+    std::once_flag once;
+    std::mutex mu;
+    cudaError_t err = cudaSuccess;
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+static SideStream g_side[64];
+
+static tt_status launch_partial_any(const AttnLaunch& L, cudaStream_t st) {
+    if (L.nd + L.np == 0) return TT_OK;
+    const int ps = prof_begin(1, st);  // the attention phase: both kernels, fork to join
+    tt_status s = TT_OK;
+    if (L.nd > 0 && L.np > 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        SideStream& S = g_side[dev & 63];
+        std::call_once(S.once, [&] {
+            S.err = cudaStreamCreateWithFlags(&S.s, cudaStreamNonBlocking);
+            if (S.err == cudaSuccess) S.err = cudaEventCreateWithFlags(&S.fork, cudaEventDisableTiming);
+            if (S.err == cudaSuccess) S.err = cudaEventCreateWithFlags(&S.join, cudaEventDisableTiming);
+        });
+        if (S.err != cudaSuccess) return check_cuda(S.err, "side stream");
+        std::lock_guard<std::mutex> g(S.mu);
+        if ((s = check_cuda(cudaEventRecord(S.fork, st), "fork")) != TT_OK) return s;
+        if ((s = check_cuda(cudaStreamWaitEvent(S.s, S.fork, 0), "fork")) != TT_OK) return s;
+        s = launch_kind(L, 0, S.s);
+        if (s == TT_OK) s = launch_kind(L, 1, st);
+        tt_status s2 = check_cuda(cudaEventRecord(S.join, S.s), "join");
+        if (s2 == TT_OK) s2 = check_cuda(cudaStreamWaitEvent(st, S.join, 0), "join");
+        if (s == TT_OK) s = s2;
+    } else {
+        s = launch_kind(L, L.nd > 0 ? 0 : 1, st);
+    }
+    prof_end(ps, st);
+    return s;
 }
 
 // The partial kernel merges a job's chunks in its last CTA when the caller

@@ -44,6 +44,8 @@ struct tt_engine {
     size_t scratch_floats = 0;
     JobDesc* job_dev = nullptr;
     void* maint_dev = nullptr;
+    int* full_map = nullptr;  // reconstruct: id -> tier slot, then the compacted id list
+    size_t full_map_n = 0;
     // host mirrors: exact (token-count driven) and upper bounds
     int h_total = 0, h_s = 0, h_rw = 0, h_rw_head = 0, h_evictions = 0;
     long long h_wr_pbs_ub = 0;  // upper bound of tokens in waiting room + PBS
@@ -384,6 +386,123 @@ __global__ void k_fill_i64(int64_t* p, size_t n, int64_t v) {
 }  // namespace tt
 
 // ---------------------------------------------------------------------------
+// full-cache reconstruction and undecayed score accumulation (the reference's
+// output_attentions path, src/tri_tier/cache.py:164-187 and :326-372)
+// ---------------------------------------------------------------------------
+// map[id - lo] = tier slot of every middle token: heavy-hitter slot i -> i,
+// live packed position p -> max_hh + p (ids are unique across tiers).
+__global__ void k_full_map(const int64_t* __restrict__ hh_ids, int hh, const int64_t* __restrict__ pbs_ids,
+                           int npbs, int max_hh, long long lo, int n, int* __restrict__ map) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < hh + npbs; i += gridDim.x * blockDim.x) {
+        const long long id = i < hh ? hh_ids[i] : pbs_ids[i - hh];
+        const long long j = id - lo;
+        if (id >= 0 && j >= 0 && j < n) map[j] = i < hh ? i : max_hh + (i - hh);
+    }
+}
+
+// One CTA: compacts the present entries of map[0..n) in id order into
+// list[0..count) (their map indices) and writes count.  1024 threads, each a
+// contiguous run, one block-wide scan of the run counts.
+__global__ void __launch_bounds__(1024) k_full_compact(const int* __restrict__ map, int n, int* __restrict__ list,
+                                                       int* __restrict__ count) {
+    __shared__ int warp_tot[32];
+    const int per = (n + blockDim.x - 1) / blockDim.x;
+    const int a = min(n, (int)threadIdx.x * per), b = min(n, a + per);
+    int c = 0;
+    for (int j = a; j < b; ++j) c += map[j] >= 0;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int t = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        warp_tot[lane] = t;  // inclusive prefix over warps
+    }
+    __syncthreads();
+    int pos = x - c + (warp > 0 ? warp_tot[warp - 1] : 0);  // exclusive prefix of this thread's run
+    for (int j = a; j < b; ++j)
+        if (map[j] >= 0) list[pos++] = j;
+    if (threadIdx.x == blockDim.x - 1) *count = pos;
+}
+
+// Rows [sinks | middle tokens by id | ring in logical order] of the full cache,
+// packed tokens dequantized as code * scale + zero with two roundings (the
+// reference's torch expression, cache.py:336-345).
+__global__ void k_full_gather(const MaintDesc* __restrict__ Ed, int S, int nmid, int rw, int head, long long total,
+                              long long lo, const int* __restrict__ map, const int* __restrict__ list,
+                              float* __restrict__ Ko, float* __restrict__ Vo, int64_t* __restrict__ ids) {
+    const MaintDesc& E = *Ed;
+    const int rows = S + nmid + rw;
+    const size_t kvs = E.kvs;
+    const int hd = E.hd;
+    for (size_t x = (size_t)blockIdx.x * blockDim.x + threadIdx.x; x < (size_t)rows * kvs;
+         x += (size_t)gridDim.x * blockDim.x) {
+        const int r = (int)(x / kvs);
+        const size_t e = x % kvs;
+        float kv, vv;
+        long long id;
+        if (r < S) {
+            kv = E.S_K[(size_t)r * kvs + e];
+            vv = E.S_V[(size_t)r * kvs + e];
+            id = r;
+        } else if (r < S + nmid) {
+            const int j = list[r - S];
+            const int slot = map[j];
+            id = lo + j;
+            if (slot < E.max_hh) {
+                kv = E.HH_K[(size_t)slot * kvs + e];
+                vv = E.HH_V[(size_t)slot * kvs + e];
+            } else {
+                const int p = slot - E.max_hh;             // packed token position
+                const int b = p / E.grp, t = p % E.grp;    // block, token within the block
+                const int h = (int)(e / hd), c = (int)(e % hd);
+                const uint32_t kw = reinterpret_cast<const uint32_t*>(E.kp)[((size_t)b * (E.grp / 16) + t / 16) * kvs + e];
+                const float ks = load_meta(E.ks, (size_t)b * kvs + e, E.meta16);
+                const float kz = load_meta(E.kz, (size_t)b * kvs + e, E.meta16);
+                kv = __fadd_rn(__fmul_rn((float)((kw >> (2 * (t % 16))) & 3u), ks), kz);
+                const uint32_t vw = reinterpret_cast<const uint32_t*>(E.vp)[((size_t)p * E.nkv + h) * E.qhd + c / 16];
+                const float vs = load_meta(E.vs, (size_t)p * E.nkv + h, E.meta16);
+                const float vz = load_meta(E.vz, (size_t)p * E.nkv + h, E.meta16);
+                vv = __fadd_rn(__fmul_rn((float)((vw >> (2 * (c % 16))) & 3u), vs), vz);
+            }
+        } else {
+            const int i = r - S - nmid;
+            const int slot = rw == E.R ? (head + i) % E.R : i;
+            kv = E.RW_K[(size_t)slot * kvs + e];
+            vv = E.RW_V[(size_t)slot * kvs + e];
+            id = rw == E.R ? total - E.R + i : (long long)S + i;
+        }
+        Ko[x] = kv;
+        Vo[x] = vv;
+        if (e == 0) ids[r] = id;
+    }
+}
+
+// g[ids[i]] += (1/H) sum_h w[h][i] for ids[i] in [0, msl) (cache.py:164-187:
+// mean over heads, index_add_ without decay).  Ids are unique, so no two
+// threads add to one entry.
+__global__ void k_accumulate_scores(float* __restrict__ g, int msl, const float* __restrict__ w,
+                                    const int64_t* __restrict__ ids, int H, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const long long id = ids ? ids[i] : i;
+        if (id < 0 || id >= msl) continue;
+        float s = 0.f;
+        for (int h = 0; h < H; ++h) s += w[(size_t)h * n + i];
+        g[id] += s / (float)H;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
 namespace {
@@ -601,6 +720,7 @@ tt_status tt_engine_destroy(tt_engine* e) {
     float* fl[] = {e->S_K, e->S_V, e->RW_K, e->RW_V, e->HH_K, e->HH_V, e->HH_scores, e->WR_K, e->WR_V, e->g, e->scratch};
     for (float* p : fl) cudaFree(p);
     cudaFree(e->HH_ids); cudaFree(e->WR_ids); cudaFree(e->ctr); cudaFree(e->job_dev); cudaFree(e->maint_dev);
+    cudaFree(e->full_map);
     free_pbs(e);
     delete e;
     return TT_OK;
@@ -885,6 +1005,113 @@ tt_status tt_engine_prefill(tt_engine* e, const float* K_all, const float* V_all
     e->h_total = q_len;
     e->last_stream = st;
     return TT_OK;
+}
+
+tt_status tt_engine_ingest(tt_engine* e, const float* K_new, const float* V_new, void* stream) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (!K_new || !V_new) return set_error(TT_ERR_INVALID_ARGUMENT, "K_new and V_new must not be NULL.");
+    if (((uintptr_t)K_new & 15) || ((uintptr_t)V_new & 15))
+        return set_error(TT_ERR_INVALID_ARGUMENT, "K_new and V_new must be 16-byte aligned.");
+    DeviceGuard dg(e->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    int dcap = 0, pcap = 0;
+    s = maintain_batch(&e, 1, &K_new, &V_new, st, dcap, pcap);
+    if (s != TT_OK) return s;
+    advance_mirrors(&e, 1, st);
+    return TT_OK;
+}
+
+tt_status tt_engine_full_count(tt_engine* e, int* count) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (!count) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_engine_counters c;
+    if ((s = tt_engine_get_counters(e, &c)) != TT_OK) return s;
+    // live packed tokens: the used blocks' ids other than -1
+    DeviceGuard dg(e->cfg.device);
+    const size_t np = (size_t)c.pbs_blocks_used * e->chunk;
+    long long live = 0;
+    if (np > 0) {
+        std::vector<int64_t> ids(np);
+        if ((s = check_cuda(cudaMemcpy(ids.data(), e->PBS_ids, np * 8, cudaMemcpyDeviceToHost), "ids")) != TT_OK)
+            return s;
+        for (int64_t v : ids) live += v != -1;
+    }
+    *count = (int)(c.s_count + c.hh_count + live + c.rw_count);
+    return TT_OK;
+}
+
+tt_status tt_engine_reconstruct(tt_engine* e, float* K_out, float* V_out, int64_t* ids_out, int capacity,
+                                int* count, void* stream) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (!K_out || !V_out || !ids_out || !count) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_engine_counters c;
+    if ((s = tt_engine_get_counters(e, &c)) != TT_OK) return s;
+    DeviceGuard dg(e->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int S = c.s_count, hh = c.hh_count, rw = c.rw_count;
+    const long long total = c.total_processed_tokens;
+    // middle ids: [S, total - rw) -- every token that left the ring
+    const long long lo = S;
+    const long long nmid_ids = std::max(0LL, total - rw - lo);
+    if (nmid_ids > (1LL << 30)) return set_error(TT_ERR_OUT_OF_RANGE, "token count overflow.");
+    const size_t need = (size_t)2 * nmid_ids + 2;  // map [n] + compacted list [n] + count
+    if (need > e->full_map_n) {
+        cudaFree(e->full_map);
+        e->full_map = nullptr;
+        e->full_map_n = 0;
+        if ((s = dalloc(&e->full_map, need, "full-cache map")) != TT_OK) return s;
+        e->full_map_n = need;
+    }
+    int* map = e->full_map;
+    int* list = map + nmid_ids;
+    int* dcount = list + nmid_ids + 1;
+    const int n = (int)nmid_ids;
+    if ((s = check_cuda(cudaMemsetAsync(map, 0xFF, (size_t)n * 4 + 4, st), "map clear")) != TT_OK) return s;
+    if ((s = check_cuda(cudaMemsetAsync(dcount, 0, 4, st), "map clear")) != TT_OK) return s;
+    const int npbs = c.pbs_blocks_used * e->chunk;
+    if (n > 0 && hh + npbs > 0) {
+        k_full_map<<<std::max(1, std::min(1184, ceil_div(hh + npbs, 256))), 256, 0, st>>>(
+            e->HH_ids, hh, e->PBS_ids, npbs, e->max_hh, lo, n, map);
+        if ((s = check_launch("k_full_map")) != TT_OK) return s;
+        k_full_compact<<<1, 1024, 0, st>>>(map, n, list, dcount);
+        if ((s = check_launch("k_full_compact")) != TT_OK) return s;
+    }
+    int nmid = 0;
+    if ((s = check_cuda(cudaMemcpyAsync(&nmid, dcount, 4, cudaMemcpyDeviceToHost, st), "count")) != TT_OK) return s;
+    if ((s = check_cuda(cudaStreamSynchronize(st), "reconstruct")) != TT_OK) return s;
+    const int rows = S + nmid + rw;
+    *count = rows;
+    if (rows > capacity)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "capacity %d is below the %d positions of the full cache.",
+                         capacity, rows);
+    if (rows > 0) {
+        const size_t work = (size_t)rows * e->kvs;
+        const int grid = (int)std::min<size_t>(148 * 8, (work + 255) / 256);
+        k_full_gather<<<std::max(1, grid), 256, 0, st>>>(reinterpret_cast<const MaintDesc*>(e->maint_dev), S, nmid,
+                                                         rw, c.rw_head_index, total, lo, map, list, K_out, V_out,
+                                                         ids_out);
+        if ((s = check_launch("k_full_gather")) != TT_OK) return s;
+    }
+    e->last_stream = st;
+    return TT_OK;
+}
+
+tt_status tt_engine_accumulate_scores(tt_engine* e, const float* weights, const int64_t* ids, int n_heads, int n,
+                                      void* stream) {
+    tt_status s = validate(e);
+    if (s != TT_OK) return s;
+    if (n < 0 || n_heads <= 0) return set_error(TT_ERR_INVALID_ARGUMENT, "n must be >= 0 and n_heads > 0.");
+    if (n == 0) return TT_OK;
+    if (!weights) return set_error(TT_ERR_INVALID_ARGUMENT, "weights must not be NULL.");
+    DeviceGuard dg(e->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    k_accumulate_scores<<<std::max(1, std::min(1184, ceil_div(n, 256))), 256, 0, st>>>(e->g, e->cfg.max_seq_len,
+                                                                                     weights, ids, n_heads, n);
+    e->last_stream = st;
+    return check_launch("k_accumulate_scores");
 }
 
 tt_status tt_engine_get_counters(tt_engine* e, tt_engine_counters* out) {

@@ -1,6 +1,7 @@
-// tt_partial.cuh -- k_attn_partial: split-KV decode attention over one chunk
-// of dense (FP32) or packed (2-bit) tokens for one kv-head group.  Included by
-// tt_attn.cu only.
+// tt_partial.cuh -- k_attn_packed: split-KV decode attention over one chunk
+// of packed (2-bit) tokens for one kv-head group, plus what it shares with the
+// dense kernel (tt_dense.cuh): small PTX helpers, the per-job chunk merge in
+// the last CTA.  Included by tt_attn.cu only.
 //
 // Packed chunks stream through shared memory in stages of 256 (token, kv-head)
 // pairs with 1-D TMA bulk copies (cp.async.bulk ... mbarrier::complete_tx),
@@ -136,21 +137,13 @@ __host__ __device__ __forceinline__ StageLayout stage_layout(int HD, int mb, int
     return s;
 }
 
-// MMA: the kernel whose packed chunks use the tensor-core unit (its warp
-// areas are MmaWarpArea; dense units only need the dense tables here).
-template <int HD, int GM, bool MMA = false>
+// Per-warp shared memory of the SIMT packed unit.
+template <int HD, int GM>
 struct WarpArea {
-    // packed units: q*scale table [half][HD][GM]; dense units reuse the same
-    // bytes for the logits transpose [token][GM] and the V row pointers
-    static constexpr int qs_packed = MMA ? 0 : 2 * HD * GM * 4;
-    static constexpr int qs_dense = 32 * GM * 4 + 32 * 8;
-    static constexpr int qs = qs_packed > qs_dense ? qs_packed : qs_dense;
+    static constexpr int qs = 2 * HD * GM * 4;  // q*scale table [half][HD][GM]
     static constexpr int ws = 32 * GM * 8;      // [token][GM] (w, w) pairs
     static constexpr int bias = 2 * 2 * GM * 4; // [half][sum qs | sum q*z][GM]
-    static constexpr int sc = 0;
-    static constexpr int vrow = 32 * GM * 4;
-    static constexpr int sum = qs + ws + bias;
-    static constexpr int bytes = sum;
+    static constexpr int bytes = qs + ws + bias;
 };
 
 template <int HD, int GM>
@@ -513,109 +506,6 @@ __device__ __forceinline__ void pbs_unit(const JobDesc& J, int HG, int G, int kv
     __syncwarp();
 }
 
-// ---------------------------------------------------------------------------
-// dense chunk: 32-token units, QK with lane <-> (token of 8, channel quarter)
-// ---------------------------------------------------------------------------
-template <int HD, int GM, class WA>
-__device__ __forceinline__ void dense_unit(const JobDesc& J, const TierCounts& tc, int G, int kvh, int lane, int ub,
-                                           int t1, const float* qk, unsigned char* wa, float sc,
-                                           WarpState<HD, GM>& S) {
-    constexpr int CPL = HDT<HD>::CPL;
-    u64* ws_tab = reinterpret_cast<u64*>(wa + WA::qs);
-    float* sc_tab = reinterpret_cast<float*>(wa + WA::sc);
-    const float** vrow = reinterpret_cast<const float**>(wa + WA::vrow);
-    const size_t kvs = (size_t)J.nkv * HD;
-    const int jt = lane >> 2, qq = lane & 3;
-    constexpr int CH = HD >= 16 ? HD / 16 : 1;  // float4 chunks per quarter
-#pragma unroll 1
-    for (int rd = 0; rd < 4; ++rd) {
-        const int tk = ub + rd * 8 + jt;
-        float a[GM];
-#pragma unroll
-        for (int g = 0; g < GM; ++g) a[g] = 0.f;
-        if (tk < t1) {
-            const float *Kb, *Vb;
-            int slot;
-            dense_slot(J, tc, tk, Kb, Vb, slot);
-            const float* krow = Kb + (size_t)slot * kvs + (size_t)kvh * HD;
-            if (qq == 0) vrow[rd * 8 + jt] = Vb + (size_t)slot * kvs + (size_t)kvh * HD;
-            float4 k4[CH];
-#pragma unroll
-            for (int i = 0; i < CH; ++i) k4[i] = __ldg(reinterpret_cast<const float4*>(krow) + 4 * i + qq);
-#pragma unroll
-            for (int i = 0; i < CH; ++i) {
-#pragma unroll
-                for (int g = 0; g < GM; ++g) {
-                    const float4 q = reinterpret_cast<const float4*>(qk + g * HD)[4 * i + qq];
-                    a[g] = fmaf(q.x, k4[i].x, a[g]);
-                    a[g] = fmaf(q.y, k4[i].y, a[g]);
-                    a[g] = fmaf(q.z, k4[i].z, a[g]);
-                    a[g] = fmaf(q.w, k4[i].w, a[g]);
-                }
-            }
-        }
-#pragma unroll
-        for (int g = 0; g < GM; ++g) {
-            a[g] += __shfl_xor_sync(0xffffffffu, a[g], 1);
-            a[g] += __shfl_xor_sync(0xffffffffu, a[g], 2);
-        }
-        if (qq == 0) {
-#pragma unroll
-            for (int g = 0; g < GM; ++g) sc_tab[(rd * 8 + jt) * GM + g] = a[g];
-        }
-    }
-    __syncwarp();
-    const int tk = ub + lane;
-    const bool inr = tk < t1;
-    float s[GM];
-#pragma unroll
-    for (int g = 0; g < GM; ++g) s[g] = inr ? sc_tab[lane * GM + g] * sc : -INFINITY;
-    if (inr) {
-#pragma unroll
-        for (int g = 0; g < GM; ++g)
-            if (g < G) J.scores[(size_t)(kvh * G + g) * J.score_stride + tk] = s[g];
-    }
-    float p[GM];
-    softmax_update<HD, GM>(S, s, p);
-#pragma unroll
-    for (int g = 0; g < GM; ++g) ws_tab[lane * GM + g] = f2pack(p[g], p[g]);
-    __syncwarp();
-    const int ntu = min(32, t1 - ub);
-    const int c0 = lane * CPL;
-#pragma unroll 16
-    for (int t = 0; t < ntu; ++t) {
-        const float* vr = vrow[t] + c0;
-        const u64* wt = ws_tab + t * GM;
-        u64 wrow[GM];
-        load_wrow<GM>(wt, wrow);
-        if constexpr (CPL >= 2) {
-            u64 v2[CPL / 2];
-            if constexpr (CPL % 4 == 0) {
-#pragma unroll
-                for (int q = 0; q < CPL / 4; ++q) {
-                    const float4 x = ldg_stream_f4(vr + 4 * q);
-                    v2[2 * q] = f2pack(x.x, x.y);
-                    v2[2 * q + 1] = f2pack(x.z, x.w);
-                }
-            } else {
-                const float2 x = __ldg(reinterpret_cast<const float2*>(vr));
-                v2[0] = f2pack(x.x, x.y);
-            }
-#pragma unroll
-            for (int g = 0; g < GM; ++g) {
-                const u64 wg = wrow[g];
-#pragma unroll
-                for (int q = 0; q < CPL / 2; ++q) S.acc2[g][q] = ffma2(wg, v2[q], S.acc2[g][q]);
-            }
-        } else {
-            const float v = c0 < HD ? __ldg(vr) : 0.f;
-#pragma unroll
-            for (int g = 0; g < GM; ++g) S.acc1[g] = fmaf(f2unpack(wt[g]).x, v, S.acc1[g]);
-        }
-    }
-    __syncwarp();
-}
-
 }  // namespace tt
 
 #include "tt_pbs_mma.cuh"
@@ -669,13 +559,12 @@ __device__ __forceinline__ void merge_warps(const JobDesc& J, const float* mbuf,
     }
 }
 
-// Shared memory of k_attn_partial<HD, GM, MMA>: the SIMT kernel's plan
+// Shared memory of k_attn_packed<HD, GM, MMA>: the SIMT kernel's plan
 // (partial_smem_bytes), or for the tensor-core kernel the query rows followed
-// by one MmaWarpArea per warp (dense chunks use the same warp areas).
+// by one MmaWarpArea per warp.
 template <int HD, int GM, bool MMA>
 __host__ __device__ __forceinline__ size_t kernel_smem_bytes(int HG, int mb) {
     if (!MMA) return partial_smem_bytes<HD, GM>(HG, mb);
-    static_assert(!MMA || WarpArea<HD, GM, true>::sum <= MmaWarpArea<HD>::bytes, "dense tables fit a warp area");
     const size_t q = (size_t)align_up(HG * GM * HD * 4, 128);
     const size_t body = (size_t)NW * MmaWarpArea<HD>::bytes;
     const size_t merge = (size_t)NW * GM * (HD + 2) * 4;
@@ -684,12 +573,12 @@ __host__ __device__ __forceinline__ size_t kernel_smem_bytes(int HG, int mb) {
 
 // MMA: packed chunks run the tensor-core unit (head_dim 64 / 128, GM <= 4, an
 // even number of kv heads, fp16 metadata: the host only selects it then);
-// dense chunks are unchanged.
+// otherwise the SIMT unit.  bx = packed chunk of the job.
 template <int HD, int GM, bool MMA>
-__device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc& J, const TierCounts tc, int bx, int by) {
+__device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& J, const TierCounts tc, int bx, int by) {
     constexpr int CPL = HDT<HD>::CPL;
     constexpr int NS = NSTAGE;  // stage slots of SIMT packed chunks
-    using WA = WarpArea<HD, GM, MMA>;
+    using WA = WarpArea<HD, GM>;
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t bars[NS];
 
@@ -698,15 +587,8 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
     const int D = tc.n0 + tc.n1 + tc.n2;
     // this launch's share of the positions (all of them unless sharded)
     const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
-    const bool is_dense = bx < L.nd;
-    int t0, t1;
-    if (is_dense) {
-        t0 = R.dlo + bx * L.DC;
-        t1 = min(R.dhi, t0 + L.DC);
-    } else {
-        t0 = R.plo + (bx - L.nd) * L.PC;
-        t1 = min(R.phi, t0 + L.PC);
-    }
+    const int t0 = R.plo + bx * L.PC;
+    const int t1 = min(R.phi, t0 + L.PC);
     if (t0 >= t1) return;
 
     const int G = L.G, HG = L.HG;
@@ -724,8 +606,8 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
 
     // SIMT packed chunks: start the first bulk copies before staging Q
     const int ST = stage_tokens(HG);
-    const int nst = is_dense ? 0 : ceil_div(t1 - t0, ST);
-    if (!MMA && !is_dense) {
+    const int nst = ceil_div(t1 - t0, ST);
+    if (!MMA) {
         if (threadIdx.x == 0) {
 #pragma unroll
             for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
@@ -748,10 +630,10 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
     const float* qk = q_s + (size_t)kvl * GM * HD;
     // partial slot: this job's active chunks, dense first, packed after (compact,
     // so a job's slots never depend on the other jobs of a batch)
-    const int chunk = is_dense ? bx : ceil_div(R.dhi - R.dlo, L.DC) + (bx - L.nd);
+    const int chunk = ceil_div(R.dhi - R.dlo, L.DC) + bx;
     float* mbuf = reinterpret_cast<float*>(smem + qbytes);  // merge buffer (aliases the stages / warp areas)
 
-    if (MMA && !is_dense) {
+    if (MMA) {
         if constexpr (MMA) {
             MmaState<HD> S;
             S.init();
@@ -824,11 +706,7 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
     WarpState<HD, GM> S;
     S.init();
     bool failed = false;
-    if (is_dense) {
-        if (active)
-            for (int u = r0; t0 + u * 32 < t1; u += WPH)
-                dense_unit<HD, GM, WA>(J, tc, G, kvh, lane, t0 + u * 32, t1, qk, wa, sc, S);
-    } else {
+    {
         int s = 0;
         for (; s < nst; ++s) {
             const bool ok = mbar_wait_bounded(&bars[s % NSTAGE], (uint32_t)((s / NSTAGE) & 1));
@@ -860,11 +738,8 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
         S.l[g] = warp_sum(S.l[g]);
-        float SW = 0.f, SZ = 0.f;
-        if (!is_dense) {
-            SW = warp_sum(S.sws[g]);
-            SZ = warp_sum(S.spz[g]);
-        }
+        const float SW = warp_sum(S.sws[g]);
+        const float SZ = warp_sum(S.spz[g]);
         if constexpr (CPL >= 2) {
 #pragma unroll
             for (int q = 0; q < CPL / 2; ++q) {
@@ -875,10 +750,8 @@ __device__ __forceinline__ void partial_body(const AttnLaunch& L, const JobDesc&
         } else {
             out[g][0] = S.acc1[g];
         }
-        if (!is_dense) {
 #pragma unroll
-            for (int j = 0; j < CPL; ++j) out[g][j] = (out[g][j] - 4.0f * SW) + SZ;
-        }
+        for (int j = 0; j < CPL; ++j) out[g][j] = (out[g][j] - 4.0f * SW) + SZ;
     }
 
     if (WPH == 1) {
@@ -1022,11 +895,11 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
     if (threadIdx.x == 0) *job_counter(J) = 0;
 }
 
-// grid (nd + np, njobs * nhg).  With merge_mode set, the job's last CTA also
-// merges the job's chunks (chunk_merge_tail); every CTA arrives, also those
-// without tokens.
+// grid (np, njobs * nhg).  With merge_mode set, the job's last CTA (of this
+// kernel or of the dense one) merges the job's chunks (chunk_merge_tail);
+// every CTA arrives, also those without tokens.
 template <int HD, int GM, bool MMA>
-__global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __grid_constant__ AttnLaunch L) {
+__global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_packed(const __grid_constant__ AttnLaunch L) {
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y / L.nhg;
@@ -1035,7 +908,7 @@ __global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_partial(const __gr
         Ts = resolve_counts(Js);
     }
     __syncthreads();
-    partial_body<HD, GM, MMA>(L, Js, Ts, blockIdx.x, blockIdx.y);
+    packed_body<HD, GM, MMA>(L, Js, Ts, blockIdx.x, blockIdx.y);
     if (L.merge_mode) chunk_merge_tail<HD>(L, Js, Ts, job);
 }
 

@@ -34,18 +34,23 @@ def _rotate_half(x: torch.Tensor) -> torch.Tensor:
 
 def _reference_attention_path(self, cache: TriTierCache, Q: torch.Tensor, num_q_heads: int, num_kv_heads: int,
                               head_dim: int):
-    """Full-weights path of patch_model.py:33-51 (needs ``output_attentions``)."""
+    """Full-weights path of patch_model.py:33-51 (``output_attentions=True``):
+    the whole cache reconstructed on the engine's device, softmax weights
+    returned and added to the accumulated scores.  Runs on the engine's device;
+    results come back on Q's device."""
     K_full, V_full, full_ids = cache.reconstruct_full_cache()
+    dev = K_full.device
+    Qd = Q.to(dev)
     if num_q_heads != num_kv_heads:
         rep = num_q_heads // num_kv_heads
         K_full = K_full.repeat_interleave(rep, dim=1)
         V_full = V_full.repeat_interleave(rep, dim=1)
-    K_full = K_full.transpose(0, 1).unsqueeze(0).to(dtype=Q.dtype)
-    V_full = V_full.transpose(0, 1).unsqueeze(0).to(dtype=Q.dtype)
+    K_full = K_full.transpose(0, 1).unsqueeze(0).to(dtype=Qd.dtype)
+    V_full = V_full.transpose(0, 1).unsqueeze(0).to(dtype=Qd.dtype)
     scaling = getattr(self, "scaling", None) or (head_dim ** -0.5)
-    w = torch.softmax(torch.matmul(Q, K_full.transpose(-2, -1)) * scaling, dim=-1)
+    w = torch.softmax(torch.matmul(Qd, K_full.transpose(-2, -1)) * scaling, dim=-1)
     cache.accumulate_attn_scrs(w, full_ids)
-    return torch.matmul(w, V_full), w
+    return torch.matmul(w, V_full).to(Q.device), w.to(Q.device)
 
 
 def patched_forward(self, hidden_states: torch.Tensor,
@@ -97,8 +102,6 @@ def patched_forward(self, hidden_states: torch.Tensor,
         return self.o_proj(ctx.transpose(1, 2).reshape(bsz, q_len, -1)), None
 
     if kwargs.get("output_attentions", False):
-        if not hasattr(cache, "reconstruct_full_cache"):
-            raise NotImplementedError("output_attentions=True needs the full-weights path")
         cache.ingest_token(K_new.squeeze(0).squeeze(1).float(), V_new.squeeze(0).squeeze(1).float())
         ctx, w = _reference_attention_path(self, cache, Q, nq, nkv, hd)
         ctx = ctx.transpose(1, 2).reshape(bsz, q_len, -1).to(dtype=hidden_states.dtype)
