@@ -15,10 +15,13 @@
 //
 // Per stage each warp takes TPW positions of its kv head (warp % HG):
 //   QK   lane <-> channels (consecutive 16-byte shared-memory reads, no bank
-//        conflicts), TPW x GM partial dots reduced with one reduce-scatter
-//        butterfly; the logits go through a small per-warp table so that
-//        every lane holds all TPW x GM of them;
-//   online softmax in log2 units, replicated in every lane (no broadcast);
+//        conflicts), f32x2 FMAs over channel pairs, the TPW x GM partial dots
+//        reduced with one reduce-scatter butterfly that leaves each logit in
+//        32 / (TPW GM) lanes;
+//   online softmax in log2 units distributed the same way (one exp per lane
+//        and head-wise max / sum over the lanes of a head); each head's
+//        rescale factor and each weight go through a per-warp table as
+//        {w, w} pairs, so the PV FMAs take them without register moves;
 //   PV   lane <-> channels, f32x2 FMAs.
 // The warps sharing a kv head merge their (m, l, acc) at the end of the chunk.
 #pragma once
@@ -38,8 +41,35 @@ template <int HD, int GM>
 __host__ __device__ __forceinline__ size_t dense_smem_bytes(int HG) {
     const size_t stages = (size_t)kDenseNS * dense_stage_bytes(HD, HG);
     const size_t merge = (size_t)NW * GM * (HD + 2) * 4;
-    const size_t tabs = (size_t)NW * kDenseTPW * GM * 4;  // per-warp logit tables
+    const size_t tabs = (size_t)NW * (kDenseTPW + 1) * GM * 8;  // per-warp {w, w} / {alpha, alpha} tables
     return (stages > merge ? stages : merge) + tabs;
+}
+
+// Sum of v[0..N) over the warp, scattered: every lane returns the total of
+// value (lane >> (5 - log2 N)); 32 / N adjacent lanes hold the same value.
+template <int N>
+__device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
+    static_assert((N & (N - 1)) == 0 && N <= 32, "power of two");
+    int cnt = N;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        if (cnt > 1) {
+            const int half = cnt / 2;
+            const bool up = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < N / 2; ++i) {
+                if (i < half) {
+                    const float send = up ? v[i] : v[i + half];
+                    const float keep = up ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            cnt = half;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+        }
+    }
+    return v[0];
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
@@ -114,32 +144,45 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
     const int NTOK = dense_stage_tokens(HG);
     const int nst = t0 < t1 ? ceil_div(t1 - t0, NTOK) : 0;
     unsigned char* stages = smem;
-    float* tab = reinterpret_cast<float*>(smem + (dense_smem_bytes<HD, GM>(HG) - (size_t)NW * NV * 4)) + warp * NV;
+    float* tab = reinterpret_cast<float*>(smem + (dense_smem_bytes<HD, GM>(HG) - (size_t)NW * (kDenseTPW + 1) * GM * 8) +
+                                          (size_t)warp * (kDenseTPW + 1) * GM * 8);
     if (warp == 0)
         for (int s = 0; s < kDenseNS && s < nst; ++s)
             dense_issue_stage<HD>(J, tc, HG, hg * HG, t0, t1, s, stages, bars, lane);
 
-    // this lane's query channels for the GM heads of its kv head (zero rows past G)
+    // this lane's query channels for the GM heads of its kv head (zero rows past
+    // G), as channel pairs for the f32x2 FMAs
     const int c0 = lane * CPL;
     const bool lane_on = c0 < HD;
-    float q[GM][CPL];
+    constexpr int NP = CPL >= 2 ? CPL / 2 : 1;  // channel pairs per lane
+    u64 q2[GM][NP];
     {
         const float* __restrict__ Qj = L.Q[job];
 #pragma unroll
-        for (int g = 0; g < GM; ++g)
+        for (int g = 0; g < GM; ++g) {
+            float qv[2 * NP];
 #pragma unroll
-            for (int j = 0; j < CPL; ++j)
-                q[g][j] = (active && g < G && lane_on) ? Qj[((size_t)kvh * G + g) * HD + c0 + j] : 0.f;
+            for (int j = 0; j < 2 * NP; ++j)
+                qv[j] = (active && g < G && lane_on && j < CPL) ? Qj[((size_t)kvh * G + g) * HD + c0 + j] : 0.f;
+#pragma unroll
+            for (int p = 0; p < NP; ++p) q2[g][p] = f2pack(qv[2 * p], qv[2 * p + 1]);
+        }
     }
     const float sc = (1.0f / sqrtf((float)HD)) * kLog2e;
-    float m[GM], l[GM], acc[GM][CPL];
+    // this lane's logit of each stage: value v = t * GM + g, held by 32 / NV lanes
+    constexpr int LOG_NV = NV >= 32 ? 5 : NV >= 16 ? 4 : NV >= 8 ? 3 : NV >= 4 ? 2 : NV >= 2 ? 1 : 0;
+    constexpr int SH = 5 - LOG_NV;
+    constexpr int LOG_GM = GM >= 8 ? 3 : GM >= 4 ? 2 : GM >= 2 ? 1 : 0;
+    const int my_v = lane >> SH, my_g = my_v & (GM - 1), my_t = my_v >> LOG_GM;
+    const bool my_first = (lane & ((1 << SH) - 1)) == 0;
+    float m_h = -INFINITY, l_h = 0.f;  // running max / sum of head my_g
+    u64 acc2[GM][NP];
 #pragma unroll
-    for (int g = 0; g < GM; ++g) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
+    for (int g = 0; g < GM; ++g)
 #pragma unroll
-        for (int j = 0; j < CPL; ++j) acc[g][j] = 0.f;
-    }
+        for (int p = 0; p < NP; ++p) acc2[g][p] = 0ull;
+    u64* wtab = reinterpret_cast<u64*>(tab);  // [TPW][GM] {w, w}, then [GM] {alpha, alpha}
+    u64* atab = wtab + kDenseTPW * GM;
     const size_t row = (size_t)HG * HD;  // floats per staged position
     bool failed = false;
     int s = 0;
@@ -160,109 +203,94 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
             float a[NV];
 #pragma unroll
             for (int t = 0; t < kDenseTPW; ++t) {
-                float k[CPL];
+                u64 k2[NP];
                 const float* kr = Ks + (size_t)(r0 + t * WPH) * row + (size_t)kvl * HD + c0;
                 if (t < ntw && lane_on) {
                     if constexpr (CPL % 4 == 0) {
 #pragma unroll
                         for (int j = 0; j < CPL; j += 4) {
-                            const float4 x = *reinterpret_cast<const float4*>(kr + j);
-                            k[j] = x.x; k[j + 1] = x.y; k[j + 2] = x.z; k[j + 3] = x.w;
+                            const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(kr + j);
+                            k2[j / 2] = x.x;
+                            k2[j / 2 + 1] = x.y;
                         }
                     } else if constexpr (CPL == 2) {
-                        const float2 x = *reinterpret_cast<const float2*>(kr);
-                        k[0] = x.x; k[1] = x.y;
+                        k2[0] = *reinterpret_cast<const u64*>(kr);
                     } else {
-                        k[0] = kr[0];
+                        k2[0] = f2pack(kr[0], 0.f);
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < CPL; ++j) k[j] = 0.f;
+                    for (int p = 0; p < NP; ++p) k2[p] = 0ull;
                 }
 #pragma unroll
                 for (int g = 0; g < GM; ++g) {
-                    float d = 0.f;
+                    u64 d = fmul2(q2[g][0], k2[0]);
 #pragma unroll
-                    for (int j = 0; j < CPL; ++j) d = fmaf(q[g][j], k[j], d);
-                    a[t * GM + g] = d;
+                    for (int p = 1; p < NP; ++p) d = ffma2(q2[g][p], k2[p], d);
+                    const float2 dd = f2unpack(d);
+                    a[t * GM + g] = dd.x + dd.y;
                 }
             }
-            warp_reduce_scatter_to_smem<NV>(a, tab, lane);
+            // ---- the lane's logit (log2 units), its head's online softmax ----
+            float sv = warp_reduce_scatter<NV>(a, lane) * sc;
+            if (my_t >= ntw || my_g >= G) sv = -INFINITY;
+            if (my_first && sv != -INFINITY)
+                J.scores[(size_t)(kvh * G + my_g) * J.score_stride + s0 + r0 + my_t * WPH] = sv;
+            float mu = sv;
+#pragma unroll
+            for (int o = 1 << (SH + LOG_GM); o < 32; o <<= 1) mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, o));
+            const float mn = fmaxf(m_h, mu);
+            const float alpha = mn == -INFINITY ? 1.f : ex2_fast(m_h - mn);
+            const float pw = sv == -INFINITY ? 0.f : ex2_fast(sv - mn);
+            float ps = pw;
+#pragma unroll
+            for (int o = 1 << (SH + LOG_GM); o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            l_h = fmaf(l_h, alpha, ps);
+            m_h = mn;
+            if (my_first) {
+                wtab[my_v] = f2pack(pw, pw);
+                if (my_t == 0) atab[my_g] = f2pack(alpha, alpha);
+            }
             __syncwarp();
-            // ---- every lane: the TPW x GM logits (log2 units) ----
-            float sl[kDenseTPW][GM];
-#pragma unroll
-            for (int t = 0; t < kDenseTPW; ++t) {
-#pragma unroll
-                for (int g = 0; g < GM; ++g) {
-                    const float v = tab[t * GM + g] * sc;
-                    sl[t][g] = (t < ntw && g < G) ? v : -INFINITY;
-                }
-            }
-            // logits to scratch for the mean weights: lane i < NV stores value i
-            if (lane < NV) {
-                const int t = lane / GM, g = lane % GM;
-                if (t < ntw && g < G)
-                    J.scores[(size_t)(kvh * G + g) * J.score_stride + s0 + r0 + t * WPH] = tab[lane] * sc;
-            }
-            __syncwarp();  // the table is rewritten next stage
-            // ---- online softmax per head ----
+            // ---- rescale and PV ----
 #pragma unroll
             for (int g = 0; g < GM; ++g) {
-                float mu = sl[0][g];
+                const u64 al = atab[g];
 #pragma unroll
-                for (int t = 1; t < kDenseTPW; ++t) mu = fmaxf(mu, sl[t][g]);
-                const float mn = fmaxf(m[g], mu);
-                float alpha = 1.f, ps = 0.f;
-                if (mn != -INFINITY) {
-                    alpha = ex2_fast(m[g] - mn);
-#pragma unroll
-                    for (int t = 0; t < kDenseTPW; ++t) {
-                        sl[t][g] = sl[t][g] == -INFINITY ? 0.f : ex2_fast(sl[t][g] - mn);
-                        ps += sl[t][g];
-                    }
-                } else {
-#pragma unroll
-                    for (int t = 0; t < kDenseTPW; ++t) sl[t][g] = 0.f;
-                }
-                m[g] = mn;
-                l[g] = fmaf(l[g], alpha, ps);
-#pragma unroll
-                for (int j = 0; j < CPL; ++j) acc[g][j] *= alpha;
+                for (int p = 0; p < NP; ++p) acc2[g][p] = fmul2(acc2[g][p], al);
             }
-            // ---- PV ----
 #pragma unroll
             for (int t = 0; t < kDenseTPW; ++t) {
                 if (t < ntw && lane_on) {
                     const float* vr = Vs + (size_t)(r0 + t * WPH) * row + (size_t)kvl * HD + c0;
-                    float v[CPL];
+                    u64 v2[NP];
                     if constexpr (CPL % 4 == 0) {
 #pragma unroll
                         for (int j = 0; j < CPL; j += 4) {
-                            const float4 x = *reinterpret_cast<const float4*>(vr + j);
-                            v[j] = x.x; v[j + 1] = x.y; v[j + 2] = x.z; v[j + 3] = x.w;
+                            const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(vr + j);
+                            v2[j / 2] = x.x;
+                            v2[j / 2 + 1] = x.y;
                         }
                     } else if constexpr (CPL == 2) {
-                        const float2 x = *reinterpret_cast<const float2*>(vr);
-                        v[0] = x.x; v[1] = x.y;
+                        v2[0] = *reinterpret_cast<const u64*>(vr);
                     } else {
-                        v[0] = vr[0];
+                        v2[0] = f2pack(vr[0], 0.f);
                     }
-                    if constexpr (CPL % 2 == 0) {
+                    u64 w[GM];
+                    if constexpr (GM % 2 == 0) {
 #pragma unroll
-                        for (int g = 0; g < GM; ++g) {
-                            const u64 pp = f2pack(sl[t][g], sl[t][g]);
-#pragma unroll
-                            for (int j = 0; j < CPL; j += 2) {
-                                const float2 r = f2unpack(ffma2(pp, f2pack(v[j], v[j + 1]), f2pack(acc[g][j], acc[g][j + 1])));
-                                acc[g][j] = r.x;
-                                acc[g][j + 1] = r.y;
-                            }
+                        for (int g = 0; g < GM; g += 2) {
+                            const ulonglong2 x = reinterpret_cast<const ulonglong2*>(wtab + t * GM)[g / 2];
+                            w[g] = x.x;
+                            w[g + 1] = x.y;
                         }
                     } else {
-#pragma unroll
-                        for (int g = 0; g < GM; ++g) acc[g][0] = fmaf(sl[t][g], v[0], acc[g][0]);
+                        w[0] = wtab[t * GM];
                     }
+#pragma unroll
+                    for (int g = 0; g < GM; ++g)
+#pragma unroll
+                        for (int p = 0; p < NP; ++p) acc2[g][p] = ffma2(w[g], v2[p], acc2[g][p]);
                 }
             }
         }
@@ -281,6 +309,18 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
         }
     } else if (t0 < t1) {
         const int chunk = (int)blockIdx.x;  // dense chunks use the first partial slots
+        float mg[GM], lg[GM], og[GM][2 * NP];
+#pragma unroll
+        for (int g = 0; g < GM; ++g) {
+            mg[g] = __shfl_sync(0xffffffffu, m_h, g << SH);  // lane of value (t = 0, g)
+            lg[g] = __shfl_sync(0xffffffffu, l_h, g << SH);
+#pragma unroll
+            for (int p = 0; p < NP; ++p) {
+                const float2 x = f2unpack(acc2[g][p]);
+                og[g][2 * p] = x.x;
+                og[g][2 * p + 1] = x.y;
+            }
+        }
         if (WPH == 1) {
             if (active) {
 #pragma unroll
@@ -288,12 +328,12 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
                     if (g >= G) break;
                     const size_t pi = part_index(J, chunk, kvh, G, g);
                     if (lane == 0) {
-                        J.part_ml[pi * 2 + 0] = m[g];
-                        J.part_ml[pi * 2 + 1] = l[g];
+                        J.part_ml[pi * 2 + 0] = mg[g];
+                        J.part_ml[pi * 2 + 1] = lg[g];
                     }
 #pragma unroll
                     for (int j = 0; j < CPL; ++j)
-                        if (lane_on) J.part_acc[pi * HD + c0 + j] = acc[g][j];
+                        if (lane_on) J.part_acc[pi * HD + c0 + j] = og[g][j];
                 }
             }
         } else {
@@ -303,12 +343,12 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
 #pragma unroll
             for (int g = 0; g < GM; ++g) {
                 if (lane == 0) {
-                    mine[g * (HD + 2) + 0] = m[g];
-                    mine[g * (HD + 2) + 1] = l[g];
+                    mine[g * (HD + 2) + 0] = mg[g];
+                    mine[g * (HD + 2) + 1] = lg[g];
                 }
 #pragma unroll
                 for (int j = 0; j < CPL; ++j)
-                    if (lane_on) mine[g * (HD + 2) + 2 + c0 + j] = acc[g][j];
+                    if (lane_on) mine[g * (HD + 2) + 2 + c0 + j] = og[g][j];
             }
             __syncthreads();
             if (r0 == 0 && active) merge_warps<HD, GM>(J, mbuf, chunk, kvh, kvl, HG, WPH, G, lane);
