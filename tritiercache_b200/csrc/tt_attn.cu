@@ -392,7 +392,9 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
         return set_error(TT_ERR_UNSUPPORTED, "head_dim %d not supported (16, 32, 64, 128, 256).", hd);
     // A kv-head group is staged as one contiguous run per region when it holds
     // every kv head (nkv <= 8); wider models split into groups of 8.
-    if (nkv <= 8) {
+    if (L.G > 4 && nkv % 4 == 0) {
+        L.HG = 4;  // the tensor-core unit runs 5..8 query heads as two warps per kv head
+    } else if (nkv <= 8) {
         L.HG = nkv;
     } else if (nkv % 8 == 0) {
         L.HG = 8;
@@ -458,12 +460,14 @@ static tt_status launch_dense_t(const AttnLaunch& L, cudaStream_t st) {
 }
 
 // Packed chunks run on the tensor cores (mma.sync f16) for head_dim 64 / 128,
-// up to 4 query heads per kv head, an even number of kv heads and fp16
-// metadata in every job of the batch; other shapes keep the SIMT unit.
+// up to 4 query heads per kv head (5 to 8 when the kv heads come in groups of
+// 4: two warps per kv head), an even number of kv heads and fp16 metadata in
+// every job of the batch; other shapes keep the SIMT unit.
 template <int HD, int GM>
 static tt_status launch_packed_g(const AttnLaunch& L, cudaStream_t st) {
-    if constexpr ((HD == 64 || HD == 128) && GM <= 4) {
-        if (L.meta_bytes == 2 && (L.HG * L.nhg) % 2 == 0) return launch_packed_t<HD, GM, true>(L, st);
+    if constexpr ((HD == 64 || HD == 128) && (GM <= 4 || GM == 8)) {
+        if (L.meta_bytes == 2 && (L.HG * L.nhg) % 2 == 0 && (GM <= 4 || L.HG == 4))
+            return launch_packed_t<HD, GM, true>(L, st);
     }
     return launch_packed_t<HD, GM, false>(L, st);
 }

@@ -7,10 +7,8 @@
 // parallelism: per stage of NTOK positions one lane of warp 0 per position
 // issues two 1-D TMA bulk copies (its K and V rows of the group's HG kv heads,
 // one contiguous span of the token's row each) into shared memory, completion
-// counted on the stage's mbarrier; NS stages are in flight, and the rows of
-// the stage NS further on are prefetched into L2 (cp.async.bulk.prefetch) as
-// each stage is issued, so about 2 NS stages of bytes are outstanding without
-// more shared memory.  Every mbarrier wait is bounded (TT_ERR_TIMEOUT recorded
+// counted on the stage's mbarrier; NS stages are in flight (an L2 prefetch of
+// the stages after them measured slower: 5.1 -> 4.4 TB/s).  Every mbarrier wait is bounded (TT_ERR_TIMEOUT recorded
 // on expiry, own copies drained).  No register holds data in flight.
 //
 // Per stage each warp takes TPW positions of its kv head (warp % HG):
@@ -72,12 +70,8 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
     return v[0];
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
-// Issues the bulk copies of stage s (positions [t0 + s*NTOK, ...) of [t0, t1))
-// and the L2 prefetch of stage s + NS.  Every copy starts 16-byte aligned (row
+// Issues the bulk copies of stage s (positions [t0 + s*NTOK, ...) of [t0, t1)).
+// Every copy starts 16-byte aligned (row
 // offsets are multiples of HD*4 bytes and the tier bases are 16-byte aligned)
 // and moves HG*HD*4 bytes.
 template <int HD>
@@ -98,15 +92,6 @@ __device__ __forceinline__ void dense_issue_stage(const JobDesc& J, const TierCo
         const size_t off = (size_t)slot * J.nkv * HD + (size_t)h0 * HD;
         tma_load_1d(buf + (size_t)lane * row, Kb + off, row, bar);
         tma_load_1d(buf + (size_t)(NTOK + lane) * row, Vb + off, row, bar);
-    }
-    const int p0 = s0 + kDenseNS * NTOK;  // the stage NS further on
-    if (lane < min(NTOK, t1 - p0)) {
-        const float *Kb, *Vb;
-        int slot;
-        dense_slot(J, tc, p0 + lane, Kb, Vb, slot);
-        const size_t off = (size_t)slot * J.nkv * HD + (size_t)h0 * HD;
-        prefetch_l2(Kb + off, row);
-        prefetch_l2(Vb + off, row);
     }
 }
 

@@ -635,18 +635,32 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
 
     if (MMA) {
         if constexpr (MMA) {
+            // More than 4 query heads per kv head (GM = 8): every kv head is
+            // two virtual halves of 4 heads, one warp each (the host then uses
+            // kv-head groups of 4, so HGv = 8 and each warp walks all units of
+            // the chunk); both halves read the same packed bytes.
+            constexpr int GS = GM > 4 ? 2 : 1;
+            constexpr int GMv = GM > 4 ? 4 : GM;
+            const int HGv = HG * GS;
+            const int vw = warp % HGv, r0v = warp / HGv, WPHv = NW / HGv;
+            const int kvl_r = vw / GS, half = vw % GS;
+            const int kvh_r = hg * HG + kvl_r;
+            const int hbase = kvh_r * G + GMv * half;           // first query head of this warp
+            const int gcnt = min(GMv, G - GMv * half);         // its query heads
+            const bool act = warp < HGv * WPHv && gcnt > 0;
+            const float* qv = q_s + (size_t)kvl_r * GM * HD + (size_t)half * GMv * HD;
             MmaState<HD> S;
             S.init();
             MmaQ<HD> Qf;
-            // This warp's units: 32-token units r0, r0 + WPH, ... of [t0, t1),
+            // This warp's units: 32-token units r0v, r0v + WPHv, ... of [t0, t1),
             // through its own kMmaSlots-deep cp.async pipeline.
             const int nu_all = ceil_div(t1 - t0, 32);
-            const int nu = active && r0 < nu_all ? ceil_div(nu_all - r0, WPH) : 0;
+            const int nu = act && r0v < nu_all ? ceil_div(nu_all - r0v, WPHv) : 0;
             if (nu > 0) {
-                mma_prepare_q<HD, GM>(qk, lane, sc, wa, Qf);
+                mma_prepare_q<HD, GMv>(qv, lane, sc, wa, Qf);
                 auto issue = [&](int k) {
-                    const int s0 = t0 + (r0 + k * WPH) * 32;
-                    mma_issue<HD>(J, kvh, s0, min(32, t1 - s0), wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes,
+                    const int s0 = t0 + (r0v + k * WPHv) * 32;
+                    mma_issue<HD>(J, kvh_r, s0, min(32, t1 - s0), wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes,
                                   lane);
                 };
 #pragma unroll
@@ -660,18 +674,19 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
                     cp_async_commit();
                     cp_async_wait<kMmaSlots - 1>();  // unit k's copies (this lane's) have landed
                     __syncwarp();                    // ... and every lane's are visible
-                    const int s0 = t0 + (r0 + k * WPH) * 32;
-                    pbs_unit_mma<HD, GM>(J, G, kvh, lane, D, wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes,
-                                         s0, min(32, t1 - s0), Qf, wa, S);
+                    const int s0 = t0 + (r0v + k * WPHv) * 32;
+                    pbs_unit_mma<HD, GMv>(J, hbase, gcnt, kvh_r, lane, D,
+                                          wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, s0, min(32, t1 - s0), Qf,
+                                          wa, S);
                 }
                 cp_async_wait<0>();
             }
             float m, l, o[HD / 16][2];
             mma_finish<HD>(S, m, l, o);
             const int gid = lane >> 2, tig = lane & 3;
-            if (WPH == 1) {
-                if (!active || tig >= G) return;
-                const size_t pi = part_index(J, chunk, kvh, G, tig);
+            if (WPHv == 1) {
+                if (!act || tig >= gcnt) return;
+                const size_t pi = (size_t)chunk * J.nq + hbase + tig;
                 if (gid == 0) {
                     J.part_ml[pi * 2 + 0] = m;
                     J.part_ml[pi * 2 + 1] = l;
@@ -683,22 +698,24 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
                 }
                 return;
             }
-            __syncthreads();
-            if (active && tig < GM) {
-                float* mine = mbuf + (size_t)warp * GM * (HD + 2) + tig * (HD + 2);
-                if (gid == 0) {
-                    mine[0] = m;
-                    mine[1] = l;
-                }
+            if constexpr (GS == 1) {  // several warps per kv head: merge them
+                __syncthreads();
+                if (active && tig < GM) {
+                    float* mine = mbuf + (size_t)warp * GM * (HD + 2) + tig * (HD + 2);
+                    if (gid == 0) {
+                        mine[0] = m;
+                        mine[1] = l;
+                    }
 #pragma unroll
-                for (int mt = 0; mt < HD / 16; ++mt) {
-                    mine[2 + 16 * mt + gid] = o[mt][0];
-                    mine[2 + 16 * mt + gid + 8] = o[mt][1];
+                    for (int mt = 0; mt < HD / 16; ++mt) {
+                        mine[2 + 16 * mt + gid] = o[mt][0];
+                        mine[2 + 16 * mt + gid + 8] = o[mt][1];
+                    }
                 }
+                __syncthreads();
+                if (r0 != 0 || !active) return;
+                merge_warps<HD, GM>(J, mbuf, chunk, kvh, kvl, HG, WPH, G, lane);
             }
-            __syncthreads();
-            if (r0 != 0 || !active) return;
-            merge_warps<HD, GM>(J, mbuf, chunk, kvh, kvl, HG, WPH, G, lane);
         }
         return;
     }
@@ -899,7 +916,7 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
 // kernel or of the dense one) merges the job's chunks (chunk_merge_tail);
 // every CTA arrives, also those without tokens.
 template <int HD, int GM, bool MMA>
-__global__ void __launch_bounds__(NT, GM >= 8 ? 1 : 2) k_attn_packed(const __grid_constant__ AttnLaunch L) {
+__global__ void __launch_bounds__(NT, (GM >= 8 && !MMA) ? 1 : 2) k_attn_packed(const __grid_constant__ AttnLaunch L) {
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
     const int job = blockIdx.y / L.nhg;

@@ -285,7 +285,9 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x (PTX ex2.approx; 
 
 // One 32-token unit [s0, s0 + nt) of kv head kvh from stage st.
 template <int HD, int GM>
-__device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, int lane, int D,
+// hbase / gcnt: the first of this warp's query heads and how many there are
+// (<= 4); kvh: the kv head whose packed bytes the unit reads.
+__device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int hbase, int gcnt, int kvh, int lane, int D,
                                              const unsigned char* st, int s0, int nt, const MmaQ<HD>& Q,
                                              unsigned char* wa, MmaState<HD>& S) {
     static_assert((HD == 64 || HD == 128) && GM <= 4, "tensor-core unit shape");
@@ -360,13 +362,13 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int G, int kvh, i
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int t = 16 * hf + gid + 8 * j;
-            const bool live = tig < G && ((live_mask >> t) & 1u);
+            const bool live = tig < gcnt && ((live_mask >> t) & 1u);
             s[2 * hf + j] = live ? ((dq[hf][2 * j] + dq[hf][2 * j + 1]) + bias) * Q.up_sc : -INFINITY;
         }
     }
     // ---- logits to scratch ----
-    if (tig < G) {
-        float* srow = J.scores + (size_t)(kvh * G + tig) * J.score_stride + D + s0;
+    if (tig < gcnt) {
+        float* srow = J.scores + (size_t)(hbase + tig) * J.score_stride + D + s0;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int t = 16 * (k >> 1) + gid + 8 * (k & 1);
