@@ -70,6 +70,8 @@ def _declare(L):
     L.orc_dequantize_v.argtypes = [vp, vp, vp, vp, i, i, i, i]
     L.orc_fused_attention_decode.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp,
                                              i, i, i, i, vp, vp, i, i]
+    L.orc_fused_attention_decode_logits.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp,
+                                                    i, i, i, i, vp, vp, i, i, vp]
     L.orc_engine_create.restype = vp
     L.orc_engine_create.argtypes = [C.POINTER(EngineParams)]
     L.orc_engine_destroy.argtypes = [vp]
@@ -119,6 +121,27 @@ def fused_attention_decode(Q, dense_K, dense_V, dense_count, kp, ks, kz, vp_, vs
     lib().orc_fused_attention_decode(_p(Q), _p(dense_K), _p(dense_V), dense_count, _p(kp), _p(ks),
                                      _p(kz), _p(vp_), _p(vs), _p(vz), _p(ids), num_blocks, nq, nkv,
                                      hd, _p(out), _p(mw), k_group_size, meta16)
+
+
+def fused_attention_logits(Q, dense_K, dense_V, dense_count, kp, ks, kz, vp_, vs, vz, ids,
+                           num_blocks, nq, nkv, hd, out, mw=None, k_group_size=16):
+    """fused_attention_decode that also returns the per-head logits [nq][T]."""
+    meta16 = _meta_fp16(ks) if ks is not None else 0
+    T = dense_count + num_blocks * k_group_size
+    logits = np.zeros((nq, max(T, 1)), np.float32)
+    lib().orc_fused_attention_decode_logits(_p(Q), _p(dense_K), _p(dense_V), dense_count, _p(kp), _p(ks),
+                                            _p(kz), _p(vp_), _p(vs), _p(vz), _p(ids), num_blocks, nq, nkv,
+                                            hd, _p(out), _p(mw), k_group_size, meta16, _p(logits))
+    return logits[:, :T]
+
+
+def mean_weights_f64(logits):
+    """The reference's head-mean softmax weights (fused_attn_avx2.cpp:286-300)
+    evaluated in double precision from its float32 logits."""
+    l = logits.astype(np.float64)
+    mx = np.max(l, axis=1, keepdims=True)
+    e = np.where(np.isfinite(l), np.exp(l - mx), 0.0)
+    return (e / e.sum(axis=1, keepdims=True)).mean(axis=0)
 
 
 _BUF_NAMES = ["S_K", "S_V", "RW_K", "RW_V", "HH_K", "HH_V", "HH_token_ids", "HH_scores", "WR_K",

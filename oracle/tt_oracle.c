@@ -285,14 +285,14 @@ static void axpy8(float* out, const float* x, float scale, int n) {
 /* ------------------------------------------------------------------ */
 /* fused decode attention: csrc/cpu/fused_attn_avx2.cpp:145-301         */
 /* ------------------------------------------------------------------ */
-void orc_fused_attention_decode(const float* Q, const float* dense_K, const float* dense_V,
-                                int dense_count, const int32_t* PBS_K_Packed,
-                                const void* PBS_K_Scales, const void* PBS_K_Zeroes,
-                                const int32_t* PBS_V_Packed, const void* PBS_V_Scales,
-                                const void* PBS_V_Zeroes, const int64_t* PBS_token_ids,
-                                int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
-                                float* attn_output, float* mean_attn_weights, int k_group_size,
-                                int meta_fp16) {
+static void fused_attention_impl(const float* Q, const float* dense_K, const float* dense_V,
+                                 int dense_count, const int32_t* PBS_K_Packed,
+                                 const void* PBS_K_Scales, const void* PBS_K_Zeroes,
+                                 const int32_t* PBS_V_Packed, const void* PBS_V_Scales,
+                                 const void* PBS_V_Zeroes, const int64_t* PBS_token_ids,
+                                 int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
+                                 float* attn_output, float* mean_attn_weights, int k_group_size,
+                                 int meta_fp16, float* logits_out) {
     const float inv_sqrt_hd = 1.0f / sqrtf((float)head_dim);               /* :166 */
     const int total_pbs = num_blocks * k_group_size;
     const int total = dense_count + total_pbs;
@@ -361,7 +361,37 @@ void orc_fused_attention_decode(const float* Q, const float* dense_K, const floa
             mean_attn_weights[i] = sw / (float)num_q_heads;
         }
     }
+    if (logits_out) memcpy(logits_out, scores, sizeof(float) * (size_t)num_q_heads * total);
     free(scores); free(kdq); free(vdq); free(row_max); free(row_sum);
+}
+
+void orc_fused_attention_decode(const float* Q, const float* dense_K, const float* dense_V,
+                                int dense_count, const int32_t* PBS_K_Packed,
+                                const void* PBS_K_Scales, const void* PBS_K_Zeroes,
+                                const int32_t* PBS_V_Packed, const void* PBS_V_Scales,
+                                const void* PBS_V_Zeroes, const int64_t* PBS_token_ids,
+                                int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
+                                float* attn_output, float* mean_attn_weights, int k_group_size,
+                                int meta_fp16) {
+    fused_attention_impl(Q, dense_K, dense_V, dense_count, PBS_K_Packed, PBS_K_Scales, PBS_K_Zeroes,
+                         PBS_V_Packed, PBS_V_Scales, PBS_V_Zeroes, PBS_token_ids, num_blocks, num_q_heads,
+                         num_kv_heads, head_dim, attn_output, mean_attn_weights, k_group_size, meta_fp16, NULL);
+}
+
+/* Same computation, also returning the per-head logits s = q.k / sqrt(hd)
+ * [num_q_heads][total] (-inf for empty packed slots): lets a test recompute
+ * the softmax normalisation in double precision. */
+void orc_fused_attention_decode_logits(const float* Q, const float* dense_K, const float* dense_V,
+                                       int dense_count, const int32_t* PBS_K_Packed,
+                                       const void* PBS_K_Scales, const void* PBS_K_Zeroes,
+                                       const int32_t* PBS_V_Packed, const void* PBS_V_Scales,
+                                       const void* PBS_V_Zeroes, const int64_t* PBS_token_ids,
+                                       int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
+                                       float* attn_output, float* mean_attn_weights, int k_group_size,
+                                       int meta_fp16, float* logits) {
+    fused_attention_impl(Q, dense_K, dense_V, dense_count, PBS_K_Packed, PBS_K_Scales, PBS_K_Zeroes,
+                         PBS_V_Packed, PBS_V_Scales, PBS_V_Zeroes, PBS_token_ids, num_blocks, num_q_heads,
+                         num_kv_heads, head_dim, attn_output, mean_attn_weights, k_group_size, meta_fp16, logits);
 }
 
 /* ------------------------------------------------------------------ */

@@ -55,6 +55,16 @@ void orc_fused_attention_decode(const float* Q, const float* dense_K, const floa
                                 float* attn_output, float* mean_attn_weights, int k_group_size,
                                 int meta_fp16);
 
+/* the same, also writing the per-head logits [num_q_heads][total] */
+void orc_fused_attention_decode_logits(const float* Q, const float* dense_K, const float* dense_V,
+                                       int dense_count, const int32_t* PBS_K_Packed,
+                                       const void* PBS_K_Scales, const void* PBS_K_Zeroes,
+                                       const int32_t* PBS_V_Packed, const void* PBS_V_Scales,
+                                       const void* PBS_V_Zeroes, const int64_t* PBS_token_ids,
+                                       int num_blocks, int num_q_heads, int num_kv_heads, int head_dim,
+                                       float* attn_output, float* mean_attn_weights, int k_group_size,
+                                       int meta_fp16, float* logits);
+
 /* csrc/include/cache_engine.h:10-123 */
 typedef struct orc_engine orc_engine;
 

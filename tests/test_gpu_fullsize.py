@@ -12,7 +12,11 @@ Tolerances:
 * mean attention weights and accumulated scores: |got - want| <=
   1e-9 + 1e-4 |want| (relative: the weights average 1/T, so an absolute
   bound of 1e-4 would accept anything at these lengths), and the weights
-  of every call sum to 1 within 1e-6;
+  of every call sum to 1 within 1e-6.  For the stand-alone attention the
+  "want" of the weights is the reference's softmax evaluated in double
+  precision from its own logits (its float32 normalisation drifts with the
+  length); the reference's float32 weights are matched within 1e-4 plus that
+  measured drift;
 * packed words, metadata bits, ids, counters and tier membership: bit-exact.
 
 Configs (bench.CONFIGS / BASELINE configs): 1 = 32q/32kv MHA at 8k (fp16 and
@@ -88,8 +92,8 @@ def attention_case(C_, O_, cfg, layer, meta):
     T = a["dc"] + a["nb"] * grp
     o_ref = np.zeros((nq, hd), np.float32)
     mw_ref = np.zeros(T, np.float32)
-    O_.fused_attention_decode(q, a["dK"], a["dV"], a["dc"], a["kp"], a["ks"], a["kz"], a["vq"], a["vs"], a["vz"],
-                              a["ids"], a["nb"], nq, nkv, hd, o_ref, mw_ref, grp)
+    logits = O_.fused_attention_logits(q, a["dK"], a["dV"], a["dc"], a["kp"], a["ks"], a["kz"], a["vq"], a["vs"],
+                                       a["vz"], a["ids"], a["nb"], nq, nkv, hd, o_ref, mw_ref, grp)
     md = (lambda x: dev(x.view(np.int16))) if meta == "fp16" else dev
     out = torch.zeros((nq, hd), device="cuda")
     mw = torch.zeros(T, device="cuda")
@@ -99,7 +103,20 @@ def attention_case(C_, O_, cfg, layer, meta):
     torch.cuda.synchronize()
     tag = f"{cfg['key']} layer {layer} {meta}"
     check_out(out.cpu().numpy(), o_ref, tag)
-    check_weights(mw.cpu().numpy(), mw_ref, tag)
+    w = mw.cpu().numpy()
+    # The reference normalises each head by a float32 sum accumulated one token
+    # at a time (fused_attn_avx2.cpp:254-259), whose relative error grows with
+    # the length (about 2e-4 at 131k tokens).  The weights are therefore held
+    # to the tolerance against the reference's softmax evaluated in double
+    # precision from its own float32 logits, and to the reference's float32
+    # weights within the tolerance plus that measured normalisation error.
+    w64 = O_.mean_weights_f64(logits)
+    check_weights(w, w64, tag + " vs float64 softmax of the reference logits")
+    live = w64 > 0
+    ref_dev = float(np.max(np.abs(mw_ref[live] - w64[live]) / w64[live])) if live.any() else 0.0
+    ok, err, bad = _within(w, mw_ref, W_ATOL, W_RTOL + ref_dev)
+    assert ok, (tag, "mean weights vs the reference's float32 weights", err, ref_dev, bad)
+    print(f"{tag}: reference float32 normalisation error {ref_dev:.2e} (relative)")
     return a
 
 
