@@ -227,38 +227,57 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
 
 /* Sequence-sharded decode step over `world` GPUs (one process per GPU).
  * Every rank holds the same engines (same configuration, same inputs every
- * step, so the same state); each rank attends a 1/world share of every
- * engine's tokens: dense positions [D*r/w, D*(r+1)/w) and packed blocks
- * [B*r/w, B*(r+1)/w).  Attention over a token set merges exactly through
- * (max, sum, weighted sum) rows, the same decomposition the reference's softmax
- * (fused_attn_avx2.cpp:245-284) allows; the reference itself has no multi-GPU
- * path.  One step is three calls, stream-ordered, around two all-gathers that
- * the caller performs with its collective library (NCCL, MPI, ...), all ranks
- * in the same order:
+ * step, so the same tier contents).  Each token has one owner rank while it
+ * stays in a tier slot: sink, heavy-hitter and ring slot j belong to rank
+ * j % world, packed tokens to ranks in granules of 256 (granule k to rank
+ * k % world).  A rank attends only the tokens it owns and alone keeps their
+ * accumulated scores current.  Attention over a token set merges exactly
+ * through (max, sum, weighted sum) rows, the decomposition the reference's
+ * softmax (fused_attn_avx2.cpp:245-284) allows; the reference itself has no
+ * multi-GPU path.  One step is two calls, stream-ordered, around two
+ * all-gathers the caller performs with its collective library (NCCL, MPI,
+ * ...), all ranks in the same order:
  *
- *   tt_engine_sharded_slot_cap(engines, n, world, &slot)     (host only)
- *   tt_engine_step_sharded_begin(..., xch_send)   maintenance + partial attention
+ *   tt_engine_step_sharded_begin(..., route_all, xch_send)
+ *       maintenance (routing from route_all) + partial attention;
  *       xch_send: n * num_q_heads * (head_dim + 2) floats (device)
  *   all-gather xch_send -> xch_all [world][n][num_q_heads][head_dim + 2]
  *       (xch_all 8-byte aligned, else TT_ERR_INVALID_ARGUMENT)
- *   tt_engine_step_sharded_merge(..., xch_all, attn_output, mw_send)
- *       attn_output identical on every rank; mw_send: n * slot floats, this
- *       rank's mean attention weights
- *   all-gather mw_send -> mw_all [world][n][slot]
- *   tt_engine_step_sharded_end(..., mw_all)       score feedback, all positions
+ *   tt_engine_step_sharded_merge(..., xch_all, attn_output, route_send)
+ *       attn_output identical on every rank; score feedback of this rank's
+ *       tokens; route_send: n routing rows of 16 bytes (device, 16-byte
+ *       aligned): the score of the token the next step evicts (from the
+ *       owner of its ring slot) and this rank's smallest heavy-hitter
+ *       (score, slot)
+ *   all-gather route_send -> route_all [world][n] rows, for the next begin.
  *
- * n <= 64.  slot must be at least what tt_engine_sharded_slot_cap returns
- * just before the step.  A rank that skips a call leaves its engines out of
+ * route_all = NULL routes from the rank's own scores, which is right when
+ * every rank holds every token's current score: after prefill, after steps
+ * that were not sharded, and after a score synchronisation.  Every
+ * update_interval tokens the maintenance recomputes the heavy-hitter
+ * threshold, a percentile over all scores (cache_engine.cpp:118-146); before
+ * such a step (tt_engine_sharded_sync_needed sets *need) the caller
+ * synchronises the scores and passes route_all = NULL (begin refuses a
+ * route_all then, with TT_ERR_INVALID_ARGUMENT):
+ *
+ *   tt_engine_sharded_scores_floats(engines, n, &f)       (host only)
+ *   tt_engine_sharded_scores_pack(..., buf)   buf[f]: the owned scores, zeros elsewhere
+ *   all-reduce (sum) buf over the ranks       exact: one nonzero term per token
+ *   tt_engine_sharded_scores_unpack(..., buf) every score current on every rank
+ *
+ * n <= 64, world <= 64.  A rank that skips a call leaves its engines out of
  * step with the others. */
-tt_status tt_engine_sharded_slot_cap(tt_engine* const* engines, int n, int world, int* slot_cap);
 tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const float* const* Q,
                                        const float* const* K_new, const float* const* V_new, int rank,
-                                       int world, int slot_cap, float* xch_send, void* stream);
-tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
-                                       const float* xch_all, float* const* attn_output, float* mw_send,
+                                       int world, const void* route_all, float* xch_send, void* stream);
+tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int rank, int world,
+                                       const float* xch_all, float* const* attn_output, void* route_send,
                                        void* stream);
-tt_status tt_engine_step_sharded_end(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
-                                     const float* mw_all, void* stream);
+tt_status tt_engine_sharded_sync_needed(tt_engine* const* engines, int n, int* need);
+tt_status tt_engine_sharded_scores_floats(tt_engine* const* engines, int n, long long* floats);
+tt_status tt_engine_sharded_scores_pack(tt_engine* const* engines, int n, int rank, int world, float* buf,
+                                        void* stream);
+tt_status tt_engine_sharded_scores_unpack(tt_engine* const* engines, int n, const float* buf, void* stream);
 
 /* Replaces TriTierCacheEngine::prefill (cache_engine.cpp:271-395; binding
  * bindings.cpp:418-436): K_all/V_all [q_len, num_kv_heads, head_dim].

@@ -546,12 +546,16 @@ def engine_step_batched(engines, Qs, Ks, Vs, outs) -> None:
 
 
 class ShardedStep:
-    """The three calls of one sequence-sharded decode step for this rank
-    (tt_engine_step_sharded_begin / _merge / _end).  Every rank holds the same
-    engines and feeds them the same inputs; each attends a 1/world share of the
-    tokens.  Between the calls the caller all-gathers, in rank order, the
-    exchange rows (`begin` -> `merge`) and the mean weights (`merge` -> `end`).
-    No reference counterpart: the reference has no multi-GPU path."""
+    """The calls of one sequence-sharded decode step for this rank
+    (tt_engine_step_sharded_begin / _merge and the score synchronisation).
+    Every rank holds the same engines and feeds them the same inputs; each
+    attends and scores the tokens it owns (ring, heavy-hitter and sink slot j
+    on rank j % world, packed tokens in 256-token granules round-robin).
+    Between begin and merge the caller all-gathers, in rank order, the exchange
+    rows; after merge the routing rows, which the next begin takes.  No
+    reference counterpart: the reference has no multi-GPU path."""
+
+    ROUTE_FLOATS = 4  # one routing row: 16 bytes
 
     def __init__(self, engines, rank: int, world: int):
         self.engines = list(engines)
@@ -560,43 +564,61 @@ class ShardedStep:
         self._hs = _handles(self.engines)
         self.nq, self.hd = self.engines[0].num_q_heads, self.engines[0].head_dim
         self.xch_floats = self.n * self.nq * (self.hd + 2)   # per rank
+        self.route_floats = self.n * self.ROUTE_FLOATS      # per rank
 
     def _ptrs(self, ts, name):
         return _ptr_array(ts, self.n, name)
 
-    def slot_cap(self) -> int:
-        """Mean-weight slots per engine this rank needs for the next step."""
+    def sync_needed(self) -> bool:
+        """Whether the next step recomputes the heavy-hitter threshold, so the
+        scores must be synchronised first (and begin gets route_all=None)."""
         v = C.c_int()
-        check(lib().tt_engine_sharded_slot_cap(self._hs, self.n, self.world, C.byref(v)), "slot_cap")
+        check(lib().tt_engine_sharded_sync_needed(self._hs, self.n, C.byref(v)), "sync_needed")
+        return bool(v.value)
+
+    def scores_floats(self) -> int:
+        v = C.c_longlong()
+        check(lib().tt_engine_sharded_scores_floats(self._hs, self.n, C.byref(v)), "scores_floats")
         return v.value
 
-    def begin(self, Qs, Ks, Vs, xch_send: torch.Tensor, slot: int) -> None:
+    def scores_pack(self, buf: torch.Tensor) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_sharded_scores_pack(self._hs, self.n, self.rank, self.world, buf.data_ptr(),
+                                                      _stream()), "scores_pack")
+
+    def scores_unpack(self, buf: torch.Tensor) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_sharded_scores_unpack(self._hs, self.n, buf.data_ptr(), _stream()),
+                  "scores_unpack")
+
+    def begin(self, Qs, Ks, Vs, xch_send: torch.Tensor, route_all: Optional[torch.Tensor]) -> None:
         with torch.cuda.device(self.engines[0]._dev):
             check(lib().tt_engine_step_sharded_begin(self._hs, self.n, self._ptrs(Qs, "Q"),
                                                      self._ptrs(Ks, "K_new"), self._ptrs(Vs, "V_new"), self.rank,
-                                                     self.world, slot, xch_send.data_ptr(), _stream()), "begin")
+                                                     self.world, None if route_all is None else route_all.data_ptr(),
+                                                     xch_send.data_ptr(), _stream()), "begin")
 
-    def merge(self, xch_all: torch.Tensor, outs, mw_send: torch.Tensor, slot: int) -> None:
+    def merge(self, xch_all: torch.Tensor, outs, route_send: torch.Tensor) -> None:
         with torch.cuda.device(self.engines[0]._dev):
-            check(lib().tt_engine_step_sharded_merge(self._hs, self.n, self.rank, self.world, slot,
-                                                     xch_all.data_ptr(), self._ptrs(outs, "attn_output"),
-                                                     mw_send.data_ptr(), _stream()), "merge")
-
-    def end(self, mw_all: torch.Tensor, slot: int) -> None:
-        with torch.cuda.device(self.engines[0]._dev):
-            check(lib().tt_engine_step_sharded_end(self._hs, self.n, self.rank, self.world, slot,
-                                                   mw_all.data_ptr(), _stream()), "end")
+            check(lib().tt_engine_step_sharded_merge(self._hs, self.n, self.rank, self.world, xch_all.data_ptr(),
+                                                     self._ptrs(outs, "attn_output"), route_send.data_ptr(),
+                                                     _stream()), "merge")
 
 
 class ShardedEngineStep:
     """engine_step_batched over the ranks of a torch.distributed process group
     (NCCL, one process per GPU), for one fixed list of engines: every rank
-    passes the same inputs and receives the same outputs; each attends 1/world
-    of the tokens.  The exchange buffers and the pointer arrays of the engines
-    are kept between calls.  With phase_timing(True) every call also records
-    CUDA events between its phases (device time per phase, phase_times())."""
+    passes the same inputs and receives the same outputs; each attends and
+    scores the tokens it owns.  Per step: begin, all-gather of the (m, l, acc)
+    rows, merge, all-gather of the routing rows; before a step that recomputes
+    the heavy-hitter threshold (every update_interval tokens) an all-reduce
+    synchronises the scores.  The first call routes from each rank's own
+    scores, which must then be current on every rank (after prefill or steps
+    that were not sharded).  The exchange buffers are kept between calls.
+    With phase_timing(True) every call also records CUDA events between its
+    phases (device time per phase, phase_times())."""
 
-    PHASES = ("begin", "allgather_rows", "merge", "allgather_weights", "end")
+    PHASES = ("sync", "begin", "allgather_rows", "merge", "allgather_route")
 
     def __init__(self, engines, rank=None, world=None, group=None):
         import torch.distributed as dist
@@ -605,22 +627,18 @@ class ShardedEngineStep:
         self.rank = dist.get_rank(group) if rank is None else int(rank)
         self.engines = list(engines)
         self.step = ShardedStep(self.engines, self.rank, self.world)
-        self.dev = torch.device("cuda", self.engines[0]._dev)
-        self.buf = None
+        self.dev = self.engines[0].device
+        st = self.step
+        self.xs = torch.empty(st.xch_floats, device=self.dev)
+        self.xa = torch.empty(self.world * st.xch_floats, device=self.dev)
+        self.rs = torch.zeros(st.route_floats, device=self.dev)
+        self.ra = torch.zeros(self.world * st.route_floats, device=self.dev)
+        self.scores = None
+        self.route_valid = False
+        self.syncs = 0
         self._timing = False
         self._acc = {p: 0.0 for p in self.PHASES}
         self._pending = []
-
-    def _buffers(self, slot):
-        b = self.buf
-        if b is None or b["slot"] < slot:
-            s = max(slot, (b["slot"] * 5 // 4) if b else slot)
-            x = self.step.xch_floats
-            n = self.step.n
-            b = {"slot": s, "xs": torch.empty(x, device=self.dev), "xa": torch.empty(self.world * x, device=self.dev),
-                 "ms": torch.empty(n * s, device=self.dev), "ma": torch.empty(self.world * n * s, device=self.dev)}
-            self.buf = b
-        return b
 
     def phase_timing(self, on: bool) -> None:
         self._timing = bool(on)
@@ -641,26 +659,32 @@ class ShardedEngineStep:
         if len(engines) != self.step.n or any(a is not b for a, b in zip(engines, self.engines)):
             raise ValueError("ShardedEngineStep: called with a different list of engines.")
         st = self.step
-        slot = st.slot_cap()
-        b = self._buffers(slot)
-        slot = b["slot"]
         ev = None
         if self._timing:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)]
             ev[0].record()
-        st.begin(Qs, Ks, Vs, b["xs"], slot)
+        route = self.ra if self.route_valid else None
+        if self.world > 1 and st.sync_needed():
+            if self.scores is None:
+                self.scores = torch.empty(st.scores_floats(), device=self.dev)
+            st.scores_pack(self.scores)
+            dist.all_reduce(self.scores, group=self.group)
+            st.scores_unpack(self.scores)
+            route = None
+            self.syncs += 1
         if ev:
             ev[1].record()
-        dist.all_gather_into_tensor(b["xa"], b["xs"], group=self.group)
+        st.begin(Qs, Ks, Vs, self.xs, route)
         if ev:
             ev[2].record()
-        st.merge(b["xa"], outs, b["ms"], slot)
+        dist.all_gather_into_tensor(self.xa, self.xs, group=self.group)
         if ev:
             ev[3].record()
-        dist.all_gather_into_tensor(b["ma"], b["ms"], group=self.group)
+        st.merge(self.xa, outs, self.rs)
         if ev:
             ev[4].record()
-        st.end(b["ma"], slot)
+        dist.all_gather_into_tensor(self.ra, self.rs, group=self.group)
+        self.route_valid = True
         if ev:
             ev[5].record()
             self._pending.append(ev)

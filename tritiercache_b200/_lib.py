@@ -61,8 +61,9 @@ EXPORTS = [
     "tt_engine_destroy", "tt_engine_step", "tt_engine_step_batched", "tt_engine_prefill",
     "tt_engine_get_counters", "tt_engine_get_buffer", "tt_engine_get_buffer_bytes",
     "tt_engine_device_bytes", "tt_engine_set_counters", "tt_profile_enable", "tt_profile_collect",
-    "tt_device_error", "tt_fused_attention_decode_noalloc", "tt_engine_sharded_slot_cap",
-    "tt_engine_step_sharded_begin", "tt_engine_step_sharded_merge", "tt_engine_step_sharded_end",
+    "tt_device_error", "tt_fused_attention_decode_noalloc", "tt_engine_step_sharded_begin",
+    "tt_engine_step_sharded_merge", "tt_engine_sharded_sync_needed", "tt_engine_sharded_scores_floats",
+    "tt_engine_sharded_scores_pack", "tt_engine_sharded_scores_unpack",
     "tt_engine_ingest", "tt_engine_full_count", "tt_engine_reconstruct", "tt_engine_accumulate_scores",
 ]
 
@@ -100,10 +101,12 @@ def _declare(L):
     L.tt_fused_attention_decode_noalloc.argtypes = [vp, vp, vp, i, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, vp, vp, i,
                                                     i, vp]
     pv = C.POINTER(vp)
-    L.tt_engine_sharded_slot_cap.argtypes = [pv, i, i, C.POINTER(i)]
-    L.tt_engine_step_sharded_begin.argtypes = [pv, i, pv, pv, pv, i, i, i, vp, vp]
-    L.tt_engine_step_sharded_merge.argtypes = [pv, i, i, i, i, vp, pv, vp, vp]
-    L.tt_engine_step_sharded_end.argtypes = [pv, i, i, i, i, vp, vp]
+    L.tt_engine_step_sharded_begin.argtypes = [pv, i, pv, pv, pv, i, i, vp, vp, vp]
+    L.tt_engine_step_sharded_merge.argtypes = [pv, i, i, i, vp, pv, vp, vp]
+    L.tt_engine_sharded_sync_needed.argtypes = [pv, i, C.POINTER(i)]
+    L.tt_engine_sharded_scores_floats.argtypes = [pv, i, C.POINTER(C.c_longlong)]
+    L.tt_engine_sharded_scores_pack.argtypes = [pv, i, i, i, vp, vp]
+    L.tt_engine_sharded_scores_unpack.argtypes = [pv, i, vp, vp]
     L.tt_engine_ingest.argtypes = [vp, vp, vp, vp]
     L.tt_engine_full_count.argtypes = [vp, C.POINTER(i)]
     L.tt_engine_reconstruct.argtypes = [vp, vp, vp, vp, i, C.POINTER(i), vp]

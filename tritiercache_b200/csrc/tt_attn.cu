@@ -174,14 +174,9 @@ __global__ void __launch_bounds__(NT, 4) k_attn_weights(const __grid_constant__ 
 // ---------------------------------------------------------------------------
 // sequence-sharded attention (see launch_sharded_* in tt_attn.cuh)
 // ---------------------------------------------------------------------------
-// Position of local index i of a rank's share (dense positions first).
-__device__ __forceinline__ int shard_pos(const ShardRange& R, int D, int i) {
-    const int nd = R.dhi - R.dlo;
-    return i < nd ? R.dlo + i : D + R.plo + (i - nd);
-}
-
-// Phase 1 epilogue: this rank's chunk partials -> one (m, l, acc) row per head.
-// grid (nq, njobs); dynamic shared memory: nd + np floats.
+// Phase 1 epilogue for launches with many chunk slots: this rank's chunk
+// partials -> one (m, l, acc) row per head.  grid (nq, njobs); dynamic shared
+// memory: nd + np + 1 floats.
 __global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant__ AttnLaunch L, float* xch) {
     extern __shared__ float wts[];
     __shared__ JobDesc Js;
@@ -197,15 +192,12 @@ __global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant_
     const JobDesc& J = Js;
     const TierCounts tc = Ts;
     const int nq = J.nq, HD = J.hd;
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
-    const int nd_act = ceil_div(R.dhi - R.dlo, L.DC), np_act = ceil_div(R.phi - R.plo, L.PC);
-    const int nch = nd_act + np_act;
+    const ShardMap SM = shard_map(tc, J.grp, L.rank, L.world);
+    const int nch = ceil_div(SM.nd, L.DC) + ceil_div(SM.np, L.PC);  // compact partial slots, dense chunks first
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto chunk_index = [](int i) { return i; };  // compact partial slots, dense chunks first
 
     float M = -INFINITY;
-    for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)chunk_index(i) * nq + h) * 2]);
+    for (int i = threadIdx.x; i < nch; i += NT) M = fmaxf(M, J.part_ml[((size_t)i * nq + h) * 2]);
     M = warp_max(M);
     if (lane == 0) red[warp] = M;
     __syncthreads();
@@ -218,7 +210,7 @@ __global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant_
     M = Mh;
     float S = 0.f;
     for (int i = threadIdx.x; i < nch; i += NT) {
-        const size_t pi = ((size_t)chunk_index(i) * nq + h) * 2;
+        const size_t pi = ((size_t)i * nq + h) * 2;
         const float mi = J.part_ml[pi];
         const float w = (M == -INFINITY || mi == -INFINITY) ? 0.f : exp2f(mi - M);
         wts[i] = w;
@@ -237,23 +229,28 @@ __global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant_
     float* dst = xch + ((size_t)job * nq + h) * (HD + 2);
     for (int c = threadIdx.x; c < HD; c += NT) {
         float o = 0.f;
-        for (int i = 0; i < nch; ++i) o = fmaf(J.part_acc[((size_t)chunk_index(i) * nq + h) * HD + c], wts[i], o);
+        for (int i = 0; i < nch; ++i) o = fmaf(J.part_acc[((size_t)i * nq + h) * HD + c], wts[i], o);
         dst[2 + c] = o;
     }
     if (threadIdx.x == 0) {
         dst[0] = M;
         dst[1] = Lh;
+        if (h == 0) *route_min_word(J) = 0ull;
     }
 }
 
 // Phase 2: every rank's rows -> output (ranks merged in order 0..world-1, so
-// all ranks produce the same bits) and this rank's mean weights.
-// grid (gx, njobs); dynamic shared memory: 2 nq floats.
+// all ranks produce the same bits), the decayed score feedback
+// g[id] = decay g[id] + w of the tokens this rank owns (cache_engine.cpp:
+// 511-540; only the owner keeps a token's score current), and the job's
+// routing row from its last CTA.  grid (gx, njobs); dynamic shared memory:
+// 2 nq floats.
 __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ AttnLaunch L, const float* xch_all,
-                                                    float* mw_send, int slot_cap) {
+                                                    RouteRow* route) {
     extern __shared__ float sm[];
     __shared__ JobDesc Js;
     __shared__ TierCounts Ts;
+    __shared__ unsigned long long red_key[NW];
     const int job = blockIdx.y;
     if (threadIdx.x == 0) Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
     __syncthreads();
@@ -314,60 +311,62 @@ __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ Attn
             out[(size_t)h * HD + c] = o;
         }
     }
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, P);
-    const int n_loc = min(slot_cap, (R.dhi - R.dlo) + (R.phi - R.plo));  // the host checked n_loc <= slot_cap
-    for (int i = blockIdx.x * NT + threadIdx.x; i < n_loc; i += gridDim.x * NT)
-        mw_send[(size_t)job * slot_cap + i] = mean_weight(J, Ms, IL, nq, shard_pos(R, D, i));
-}
-
-// Phase 3: every rank's mean weights -> score feedback for all positions.
-// grid (ceil(slot_cap / (NT * kFeedbackPer)), njobs, world); each thread
-// updates kFeedbackPer positions (slots x*kFeedbackPer*NT + k*NT + thread),
-// with every load (weights, token ids, old scores) issued before its stores,
-// so a CTA pays the dependent-load chain once for several positions.
-constexpr int kFeedbackPer = 4;
-__global__ void __launch_bounds__(NT) k_shard_feedback(const __grid_constant__ AttnLaunch L, const float* mw_all,
-                                                       int slot_cap) {
-    __shared__ JobDesc Js;
-    __shared__ TierCounts Ts;
-    const int job = blockIdx.y, p = blockIdx.z;
-    int idx[kFeedbackPer];
-    float w[kFeedbackPer];
-    const float* mwr = mw_all + ((size_t)p * L.njobs + job) * slot_cap;
+    // feedback of this rank's positions; the heavy-hitter minimum over them
+    const int r = L.rank;
+    const ShardMap SM = shard_map(tc, J.grp, r, P);
+    const int n_loc = SM.nd + SM.np;
+    unsigned long long best = 0ull;  // complemented key, 0 = none
+    if (J.g) {
+        for (int i = blockIdx.x * NT + threadIdx.x; i < n_loc; i += gridDim.x * NT) {
+            int hh;
+            long long id = local_position_id(J, tc, SM, r, P, i, hh);
+            const bool fb = id >= 0 && id < J.msl;
+            const float g_old = fb ? J.g[id] : 0.f;
+            const float w = mean_weight(J, Ms, IL, nq, i);
+            if (!fb) continue;
+            const float nv = fmaf(J.decay, g_old, w);
+            J.g[id] = nv;
+            if (hh >= 0) {
+                J.hh_scores[hh] = nv;
+                const unsigned long long key = ~(((unsigned long long)order_key(nv) << 32) | (uint32_t)hh);
+                best = key > best ? key : best;
+            }
+        }
+    }
 #pragma unroll
-    for (int k = 0; k < kFeedbackPer; ++k) {  // the weights do not depend on the descriptor chain
-        idx[k] = (blockIdx.x * kFeedbackPer + k) * NT + threadIdx.x;
-        w[k] = idx[k] < slot_cap ? mwr[idx[k]] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
     }
-    if (threadIdx.x == 0) {
-        Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
-        Ts = resolve_counts(Js);
-    }
+    if ((threadIdx.x & 31) == 0) red_key[threadIdx.x >> 5] = best;
+    __shared__ int last;
     __syncthreads();
-    const JobDesc& J = Js;
-    const TierCounts tc = Ts;
-    if (!J.g) return;
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const ShardRange R = shard_range(D, tc.nblk, J.grp, p, L.world);
-    const int n_loc = min(slot_cap, (R.dhi - R.dlo) + (R.phi - R.plo));
-    long long id[kFeedbackPer];
-    int hh[kFeedbackPer];
-#pragma unroll
-    for (int k = 0; k < kFeedbackPer; ++k) {
-        hh[k] = -1;
-        id[k] = idx[k] < n_loc ? position_id(J, tc, D, shard_pos(R, D, idx[k]), hh[k]) : -1;
-        if (id[k] >= J.msl) id[k] = -1;
-    }
-    float g0[kFeedbackPer];
-#pragma unroll
-    for (int k = 0; k < kFeedbackPer; ++k) g0[k] = id[k] >= 0 ? J.g[id[k]] : 0.f;
-#pragma unroll
-    for (int k = 0; k < kFeedbackPer; ++k) {  // positions hold distinct tokens: no two updates meet
-        if (id[k] < 0) continue;
-        const float nv = fmaf(J.decay, g0[k], w[k]);
-        J.g[id[k]] = nv;
-        if (hh[k] >= 0) J.hh_scores[hh[k]] = nv;
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < NW; ++w) best = red_key[w] > best ? red_key[w] : best;
+        if (best) atomicMax(route_min_word(J), best);
+        __threadfence();
+        last = atomicAdd(job_counter(J), 1) == (int)gridDim.x - 1;
+        if (last) {
+            __threadfence();
+            const unsigned long long k = atomicExch(route_min_word(J), 0ull);
+            RouteRow rr;
+            rr.ev_score = 0.f;
+            rr.hh_min = 0.f;
+            rr.hh_slot = -1;
+            rr.pad = 0;
+            if (k) {
+                const unsigned long long key = ~k;
+                rr.hh_min = key_value((uint32_t)(key >> 32));
+                rr.hh_slot = (int)(uint32_t)key;
+            }
+            // the token the next step evicts: ring slot ring_head, id total - R
+            if (J.g && tc.ring_size > 0 && tc.n2 == tc.ring_size && tc.ring_head % P == r) {
+                const long long id = (long long)tc.total - tc.ring_size;
+                if (id >= 0 && id < J.msl) rr.ev_score = __ldcg(J.g + id);
+            }
+            route[job] = rr;
+            *job_counter(J) = 0;
+        }
     }
 }
 
@@ -566,22 +565,15 @@ tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t s
     return check_launch("k_shard_local_merge");
 }
 
-tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, float* mw_send, int slot_cap,
+tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, RouteRow* route, int pos_cap,
                                cudaStream_t st) {
-    const int gx = std::max(L.inline_job.nq, ceil_div(slot_cap, 4 * NT));
+    // about 8 CTAs per SM over the launch for the feedback, at least one per head
+    const int gx = std::max(L.inline_job.nq, std::min(ceil_div(std::max(pos_cap, 1), NT), std::max(1, 8 * 148 / L.njobs)));
     dim3 grid(gx, L.njobs);
     const int ps = prof_begin(2, st);
-    k_shard_merge<<<grid, NT, (size_t)2 * L.inline_job.nq * sizeof(float), st>>>(L, xch_all, mw_send, slot_cap);
+    k_shard_merge<<<grid, NT, (size_t)2 * L.inline_job.nq * sizeof(float), st>>>(L, xch_all, route);
     prof_end(ps, st);
     return check_launch("k_shard_merge");
-}
-
-tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int slot_cap, cudaStream_t st) {
-    dim3 grid(std::max(1, ceil_div(slot_cap, NT * kFeedbackPer)), L.njobs, L.world);
-    const int ps = prof_begin(2, st);
-    k_shard_feedback<<<grid, NT, 0, st>>>(L, mw_all, slot_cap);
-    prof_end(ps, st);
-    return check_launch("k_shard_feedback");
 }
 
 // L.inline_job.hd / .nq must be set for engine batches too (they select the

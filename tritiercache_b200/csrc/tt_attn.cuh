@@ -1,6 +1,8 @@
 // tt_attn.cuh -- job description shared by the fused decode attention
 // kernels (tt_attn.cu) and the cache engine (tt_engine.cu).
 #pragma once
+#include <string.h>
+
 #include "tt_common.cuh"
 
 namespace tt {
@@ -105,41 +107,102 @@ struct AttnLaunch {
 // shapes the kernels are not built for.
 tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, int pbs_tok_cap);
 
-// The tokens one rank of `world` attends: dense positions [dlo, dhi) and
-// packed token offsets [plo, phi) (whole blocks).  Every rank derives the same
-// split from the same (replicated) counters.
-struct ShardRange {
-    int dlo, dhi, plo, phi;
+// Sequence sharding over `world` ranks.  Every token has one owner rank for
+// as long as it stays in one tier slot: sink, heavy-hitter and ring slot j
+// belong to rank j mod world, the packed tier to ranks in granules of
+// kShardGran tokens (granule k to rank k mod world).  A rank attends exactly
+// the tokens it owns and alone keeps their accumulated scores up to date, so
+// the ranks need not exchange per-position weights.  A rank's positions are
+// numbered locally: its dense positions first (its sinks, then its heavy
+// hitters, then its ring slots, in slot order), then its packed tokens in
+// granule order.  world <= 1: local = global numbering.
+constexpr int kShardGran = 256;
+
+__host__ __device__ __forceinline__ int owned_count(int n, int r, int w) { return n > r ? (n - r + w - 1) / w : 0; }
+
+struct ShardMap {
+    int nd, np;  // this rank's dense positions and packed tokens
 };
-__host__ __device__ __forceinline__ ShardRange shard_range(int D, int nblk, int grp, int rank, int world) {
-    ShardRange r;
-    if (world <= 1) {
-        r.dlo = 0; r.dhi = D; r.plo = 0; r.phi = nblk * grp;
-    } else {
-        r.dlo = (int)((long long)D * rank / world);
-        r.dhi = (int)((long long)D * (rank + 1) / world);
-        r.plo = (int)((long long)nblk * rank / world) * grp;
-        r.phi = (int)((long long)nblk * (rank + 1) / world) * grp;
+__host__ __device__ __forceinline__ ShardMap shard_map(const TierCounts& tc, int grp, int r, int w) {
+    ShardMap m;
+    const int P = tc.nblk * grp;
+    if (w <= 1) {
+        m.nd = tc.n0 + tc.n1 + tc.n2;
+        m.np = P;
+        return m;
     }
-    return r;
+    m.nd = owned_count(tc.n0, r, w) + owned_count(tc.n1, r, w) + owned_count(tc.n2, r, w);
+    const int ng = (P + kShardGran - 1) / kShardGran;
+    const int cnt = owned_count(ng, r, w);
+    m.np = cnt * kShardGran;
+    if (cnt > 0 && (ng - 1) % w == r) m.np -= ng * kShardGran - P;  // this rank holds the partial last granule
+    return m;
 }
+// Global packed token of local packed token i.
+__host__ __device__ __forceinline__ int packed_global(int i, int r, int w) {
+    return w <= 1 ? i : ((i / kShardGran) * w + r) * kShardGran + i % kShardGran;
+}
+// Tier (0 sinks, 1 heavy hitters, 2 ring) and slot of local dense position i.
+__host__ __device__ __forceinline__ int dense_local_slot(const TierCounts& tc, int i, int r, int w, int& slot) {
+    if (w <= 1) {
+        if (i < tc.n0) { slot = i; return 0; }
+        if (i < tc.n0 + tc.n1) { slot = i - tc.n0; return 1; }
+        const int q = i - tc.n0 - tc.n1;
+        slot = tc.ring_size > 0 ? (tc.ring_head + q) % tc.ring_size : q;  // logical ring order
+        return 2;
+    }
+    const int a = owned_count(tc.n0, r, w), b = owned_count(tc.n1, r, w);
+    if (i < a) { slot = r + w * i; return 0; }
+    if (i < a + b) { slot = r + w * (i - a); return 1; }
+    slot = r + w * (i - a - b);
+    return 2;
+}
+// Ring slot -> token id: the ring holds ids [total - n2, total), the oldest
+// at ring_head (ring_head is 0 while the ring fills).
+__host__ __device__ __forceinline__ long long ring_slot_id(const TierCounts& tc, int slot) {
+    int q = slot - tc.ring_head;
+    if (q < 0) q += tc.ring_size;
+    return (long long)tc.total - tc.n2 + q;
+}
+
+// Total order of floats as unsigned keys (negative values reversed), and back.
+__host__ __device__ __forceinline__ uint32_t order_key(float x) {
+    uint32_t b;
+    memcpy(&b, &x, 4);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__host__ __device__ __forceinline__ float key_value(uint32_t k) {
+    const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    float x;
+    memcpy(&x, &b, 4);
+    return x;
+}
+
+// Routing row a rank publishes after a sharded step, for the next step's
+// maintenance on every rank: the accumulated score of the token the next
+// step evicts (valid from the owner of ring slot ring_head) and the smallest
+// (score, slot) over this rank's heavy-hitter slots (slot -1: none).
+struct RouteRow {
+    float ev_score;
+    float hh_min;
+    int hh_slot;
+    int pad;
+};
+
 // Scratch a job needs for a given plan: chunk slots and score stride.
 int attn_max_chunks(int dense_cap, int pbs_tok_cap);
 // Launches the partial, head-merge and weights kernels on `stream`.
 tt_status launch_attention(const AttnLaunch& L, cudaStream_t stream);
 
-// Sequence-sharded attention, three stream-ordered phases around two
-// all-gathers done by the caller (L.rank / L.world set, L.mw unused):
-//  1. partial attention over this rank's share, merged into one
+// Sequence-sharded attention, two stream-ordered phases around an all-gather
+// done by the caller (L.rank / L.world set, L.mw unused):
+//  1. partial attention over the tokens this rank owns, merged into one
 //     (m, l, acc[hd]) row per (job, head): xch[job][h][hd + 2];
 //  2. given every rank's rows (xch_all[world][njobs][nq][hd + 2]): the output
-//     (same arithmetic and order on every rank) and the mean attention weights
-//     of this rank's positions: mw_send[job][slot_cap];
-//  3. given every rank's weights (mw_all[world][njobs][slot_cap]): score
-//     feedback for all positions, identical on every rank.
+//     (same arithmetic and order on every rank), the score feedback of this
+//     rank's tokens and its routing row route[job] for the next step.
 tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t stream);
-tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, float* mw_send, int slot_cap,
+tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, RouteRow* route, int pos_cap,
                                cudaStream_t stream);
-tt_status launch_sharded_feedback(const AttnLaunch& L, const float* mw_all, int slot_cap, cudaStream_t stream);
 
 }  // namespace tt

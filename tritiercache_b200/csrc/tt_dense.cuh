@@ -76,7 +76,8 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
 // and moves HG*HD*4 bytes.
 template <int HD>
 __device__ __forceinline__ void dense_issue_stage(const JobDesc& J, const TierCounts& tc, int HG, int h0, int t0,
-                                                  int t1, int s, unsigned char* stages, uint64_t* bars, int lane) {
+                                                  int t1, int s, unsigned char* stages, uint64_t* bars, int lane,
+                                                  int rank, int world) {
     const int NTOK = dense_stage_tokens(HG);
     const int s0 = t0 + s * NTOK;
     const int nt = min(NTOK, t1 - s0);
@@ -88,7 +89,7 @@ __device__ __forceinline__ void dense_issue_stage(const JobDesc& J, const TierCo
     if (lane < nt) {
         const float *Kb, *Vb;
         int slot;
-        dense_slot(J, tc, s0 + lane, Kb, Vb, slot);
+        dense_slot(J, tc, s0 + lane, rank, world, Kb, Vb, slot);
         const size_t off = (size_t)slot * J.nkv * HD + (size_t)h0 * HD;
         tma_load_1d(buf + (size_t)lane * row, Kb + off, row, bar);
         tma_load_1d(buf + (size_t)(NTOK + lane) * row, Vb + off, row, bar);
@@ -117,10 +118,9 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
     __syncthreads();
     const JobDesc& J = Js;
     const TierCounts tc = Ts;
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
-    const int t0 = R.dlo + (int)blockIdx.x * L.DC;
-    const int t1 = min(R.dhi, t0 + L.DC);
+    const ShardMap M = shard_map(tc, J.grp, L.rank, L.world);
+    const int t0 = (int)blockIdx.x * L.DC;  // this rank's local dense positions [t0, t1)
+    const int t1 = min(M.nd, t0 + L.DC);
     const int G = L.G, HG = L.HG;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int kvl = warp % HG, r0 = warp / HG, WPH = NW / HG;
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
                                           (size_t)warp * (kDenseTPW + 1) * GM * 8);
     if (warp == 0)
         for (int s = 0; s < kDenseNS && s < nst; ++s)
-            dense_issue_stage<HD>(J, tc, HG, hg * HG, t0, t1, s, stages, bars, lane);
+            dense_issue_stage<HD>(J, tc, HG, hg * HG, t0, t1, s, stages, bars, lane, L.rank, L.world);
 
     // this lane's query channels for the GM heads of its kv head (zero rows past
     // G), as channel pairs for the f32x2 FMAs
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
         }
         __syncthreads();  // every warp is done with this slot
         if (warp == 0 && s + kDenseNS < nst)
-            dense_issue_stage<HD>(J, tc, HG, hg * HG, t0, t1, s + kDenseNS, stages, bars, lane);
+            dense_issue_stage<HD>(J, tc, HG, hg * HG, t0, t1, s + kDenseNS, stages, bars, lane, L.rank, L.world);
     }
     if (failed) {
         // drain this CTA's own copies in flight and give up on the chunk (it

@@ -48,6 +48,7 @@ struct tt_engine {
     size_t full_map_n = 0;
     // host mirrors: exact (token-count driven) and upper bounds
     int h_total = 0, h_s = 0, h_rw = 0, h_rw_head = 0, h_evictions = 0;
+    int h_last_calc = -1;  // last_calc_pos: the steps that recompute the threshold
     long long h_wr_pbs_ub = 0;  // upper bound of tokens in waiting room + PBS
     cudaStream_t last_stream = nullptr;
 };
@@ -68,6 +69,11 @@ struct MaintDesc {
 
 struct MaintBatch {
     int n;
+    // Sequence-sharded steps: the ranks' routing rows [world][n] of the last
+    // step (nullptr: route from this engine's own scores, which are then
+    // current for every token).
+    const RouteRow* route;
+    int world;
     const MaintDesc* d[kMaxBatch];
     const float* K[kMaxBatch];
     const float* V[kMaxBatch];
@@ -83,14 +89,6 @@ __device__ __forceinline__ void copy_row(float* __restrict__ dst, const float* _
     } else {
         for (size_t i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
     }
-}
-
-__device__ __forceinline__ uint32_t order_key(float x) {
-    const uint32_t b = __float_as_uint(x);
-    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float key_value(uint32_t k) {
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
 // k-th smallest (0-based) of x[0..n): 4 passes of an 8-bit radix histogram.
@@ -205,7 +203,14 @@ __global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ 
         __syncthreads();
         if (threadIdx.x == 0) {
             c.total_evictions++;
-            s_score = (id >= 0 && id < E.msl) ? E.g[id] : 0.f;
+            if (B.route) {
+                // the ring slot's owner published the score; every rank stores
+                // it, so the token's score is current wherever it moves next
+                s_score = B.route[(size_t)(slot % B.world) * B.n + blockIdx.x].ev_score;
+                if (id >= 0 && id < E.msl) E.g[id] = s_score;
+            } else {
+                s_score = (id >= 0 && id < E.msl) ? E.g[id] : 0.f;
+            }
         }
         __syncthreads();
         const float score = s_score, thresh = c.cached_threshold;
@@ -214,6 +219,29 @@ __global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ 
         if (score >= thresh) {
             if (c.hh_count < E.max_hh) {
                 action = 0;
+            } else if (B.route) {
+                // global strict-< argmin, first slot wins: the smallest
+                // (score, slot) over the ranks' minima of their own slots
+                if (threadIdx.x == 0) {
+                    float v0 = INFINITY;
+                    int i0 = -1;
+                    for (int p = 0; p < B.world; ++p) {
+                        const RouteRow rr = B.route[(size_t)p * B.n + blockIdx.x];
+                        if (rr.hh_slot >= 0 && (i0 < 0 || rr.hh_min < v0 || (rr.hh_min == v0 && rr.hh_slot < i0))) {
+                            v0 = rr.hh_min;
+                            i0 = rr.hh_slot;
+                        }
+                    }
+                    s_mi = i0 < 0 ? 0 : i0;
+                    s_action = (i0 >= 0 && score > v0) ? 1 : 2;
+                    if (s_action == 1) {  // the demoted token's current score (its owner's HH_scores entry)
+                        const long long did = E.HH_ids[i0];
+                        if (did >= 0 && did < E.msl) E.g[did] = v0;
+                    }
+                }
+                __syncthreads();
+                action = s_action;
+                mi = s_mi;
             } else {
                 // strict-< argmin, first index wins (:231-238)
                 float bv = INFINITY;
@@ -503,6 +531,55 @@ __global__ void k_accumulate_scores(float* __restrict__ g, int msl, const float*
 }
 
 // ---------------------------------------------------------------------------
+// score synchronisation of sequence-sharded steps
+// ---------------------------------------------------------------------------
+// buf[id] = g[id] for the tokens rank `r` of `w` owns (zero elsewhere; the
+// caller zeroes buf): its sink, heavy-hitter and ring slots (slot % w == r),
+// its packed granules, and on rank 0 the waiting room, whose scores every
+// rank holds.  Summed over the ranks, buf is every token's current score.
+__global__ void __launch_bounds__(256) k_scores_pack(const MaintDesc* __restrict__ Ed, int r, int w,
+                                                     float* __restrict__ buf) {
+    const MaintDesc& E = *Ed;
+    const DevCounters c = *E.ctr;
+    TierCounts tc;
+    tc.n0 = c.s_count; tc.n1 = c.hh_count; tc.n2 = c.rw_count; tc.ring_head = c.rw_head; tc.ring_size = E.R;
+    tc.nblk = c.pbs_used; tc.total = c.total;
+    const long long nS = E.S, nH = E.max_hh, nR = E.R, nW = E.grp;
+    const long long nP = (long long)c.pbs_used * E.grp;
+    const long long items = nS + nH + nR + nW + nP;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < items;
+         i += (long long)gridDim.x * blockDim.x) {
+        long long id = -1;
+        if (i < nS) {
+            if (i < tc.n0 && i % w == r) id = i;
+        } else if (i < nS + nH) {
+            const int k = (int)(i - nS);
+            if (k < tc.n1 && k % w == r) id = E.HH_ids[k];
+        } else if (i < nS + nH + nR) {
+            const int k = (int)(i - nS - nH);
+            if (k < tc.n2 && k % w == r) id = ring_slot_id(tc, k);
+        } else if (i < nS + nH + nR + nW) {
+            const int k = (int)(i - nS - nH - nR);
+            if (k < c.wr_count && r == 0) id = E.WR_ids[k];
+        } else {
+            const long long p = i - nS - nH - nR - nW;
+            if ((p / kShardGran) % w == r) id = E.PBS_ids[p];
+        }
+        if (id >= 0 && id < E.msl) buf[id] = E.g[id];
+    }
+}
+
+// HH_scores[i] = g[HH_ids[i]]: the heavy hitters' copy of the synchronised scores.
+__global__ void k_scores_refresh_hh(const MaintDesc* __restrict__ Ed) {
+    const MaintDesc& E = *Ed;
+    const int n = E.ctr->hh_count;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const long long id = E.HH_ids[i];
+        if (id >= 0 && id < E.msl) E.HH_scores[i] = E.g[id];
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------
 namespace {
@@ -764,10 +841,12 @@ long long step_block_bound(const tt_engine* e) {
 // Maintenance of engines[0..m) in one launch; returns the dense and packed
 // token capacities the attention launch must cover.
 tt_status maintain_batch(tt_engine* const* engines, int m, const float* const* K_new, const float* const* V_new,
-                         cudaStream_t st, int& dcap, int& pcap) {
+                         cudaStream_t st, int& dcap, int& pcap, const RouteRow* route = nullptr, int world = 1) {
     MaintBatch mb;
     memset(&mb, 0, sizeof(mb));
     mb.n = m;
+    mb.route = route;
+    mb.world = world;
     dcap = 0;
     pcap = 0;
     for (int i = 0; i < m; ++i) {
@@ -814,6 +893,10 @@ void advance_mirrors(tt_engine* const* engines, int m, cudaStream_t st) {
         } else if (e->h_rw < e->cfg.rw_size) {
             e->h_rw++;
         } else {
+            const int ce = e->h_total - e->cfg.rw_size;  // threshold schedule of k_engine_maintain
+            if (ce > e->cfg.sink_size &&
+                (e->h_last_calc == -1 || e->h_total - e->h_last_calc >= e->cfg.update_interval))
+                e->h_last_calc = e->h_total;
             e->h_rw_head = (e->h_rw_head + 1) % e->cfg.rw_size;
             e->h_evictions++;
             e->h_wr_pbs_ub++;
@@ -823,17 +906,27 @@ void advance_mirrors(tt_engine* const* engines, int m, cudaStream_t st) {
     }
 }
 
-// Positions one rank of `world` may hold in the next step (slot capacity).
-long long shard_slot_need(const tt_engine* e, int world) {
-    return (long long)ceil_div(dense_cap(e), world) + (step_block_bound(e) + world - 1) / world * e->chunk;
+// Does the next step of e recompute the heavy-hitter threshold (host mirror
+// of k_engine_maintain's schedule)?
+bool step_recomputes_threshold(const tt_engine* e) {
+    if (!step_evicts(e)) return false;
+    return e->h_total - e->cfg.rw_size > e->cfg.sink_size &&
+           (e->h_last_calc == -1 || e->h_total - e->h_last_calc >= e->cfg.update_interval);
 }
 
-tt_status validate_shard_args(tt_engine* const* engines, int n, int rank, int world, int slot_cap) {
+// One rank's share of a sharded launch: at most ceil(n / world) slots of each
+// dense tier and ceil(granules / world) packed granules.
+void shard_caps(const tt_engine* e, long long blocks, int world, int& dcap_r, int& pcap_r) {
+    dcap_r = ceil_div(e->cfg.sink_size, world) + ceil_div(e->max_hh, world) + ceil_div(e->cfg.rw_size, world);
+    const long long gran = (std::min<long long>(blocks, e->pbs_cap) * e->chunk + kShardGran - 1) / kShardGran;
+    pcap_r = (int)((gran + world - 1) / world) * kShardGran;
+}
+
+tt_status validate_shard_args(tt_engine* const* engines, int n, int rank, int world) {
     if (!engines) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
     if (n > kMaxBatch) return set_error(TT_ERR_INVALID_ARGUMENT, "a sharded step takes at most %d engines.", kMaxBatch);
-    if (world < 1 || rank < 0 || rank >= world)
-        return set_error(TT_ERR_INVALID_ARGUMENT, "rank %d / world %d out of range.", rank, world);
-    if (slot_cap < 0) return set_error(TT_ERR_INVALID_ARGUMENT, "slot_cap must be non-negative.");
+    if (world < 1 || world > 64 || rank < 0 || rank >= world)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "rank %d / world %d out of range (world <= 64).", rank, world);
     for (int i = 0; i < n; ++i) {
         tt_status s = validate(engines[i]);
         if (s != TT_OK) return s;
@@ -876,47 +969,115 @@ tt_status tt_engine_step_batched(tt_engine* const* engines, int n, const float* 
     return TT_OK;
 }
 
-tt_status tt_engine_sharded_slot_cap(tt_engine* const* engines, int n, int world, int* slot_cap) {
-    if (!engines || !slot_cap) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
-    if (world < 1) return set_error(TT_ERR_INVALID_ARGUMENT, "world must be at least 1.");
-    long long need = 0;
+tt_status tt_engine_sharded_sync_needed(tt_engine* const* engines, int n, int* need) {
+    if (!engines || !need) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    *need = 0;
     for (int i = 0; i < n; ++i) {
         tt_status s = validate(engines[i]);
         if (s != TT_OK) return s;
-        need = std::max(need, shard_slot_need(engines[i], world));
+        if (step_recomputes_threshold(engines[i])) *need = 1;
     }
-    if (need > (1LL << 30)) return set_error(TT_ERR_INVALID_ARGUMENT, "slot capacity overflow.");
-    *slot_cap = (int)need;
+    return TT_OK;
+}
+
+tt_status tt_engine_sharded_scores_floats(tt_engine* const* engines, int n, long long* floats) {
+    if (!engines || !floats) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    long long t = 0;
+    for (int i = 0; i < n; ++i) {
+        tt_status s = validate(engines[i]);
+        if (s != TT_OK) return s;
+        t += engines[i]->cfg.max_seq_len;
+    }
+    *floats = t;
+    return TT_OK;
+}
+
+tt_status tt_engine_sharded_scores_pack(tt_engine* const* engines, int n, int rank, int world, float* buf,
+                                        void* stream) {
+    if (n <= 0) return TT_OK;
+    tt_status s = validate_shard_args(engines, n, rank, world);
+    if (s != TT_OK) return s;
+    if (!buf) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    DeviceGuard dg(engines[0]->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        tt_engine* e = engines[i];
+        const size_t msl = (size_t)e->cfg.max_seq_len;
+        if ((s = check_cuda(cudaMemsetAsync(buf + off, 0, msl * sizeof(float), st), "scores pack")) != TT_OK) return s;
+        const long long items = (long long)dense_cap(e) + e->chunk + (long long)e->pbs_cap * e->chunk;
+        const int grid = (int)std::min<long long>((items + 255) / 256, 4 * 148);
+        k_scores_pack<<<grid, 256, 0, st>>>(reinterpret_cast<const MaintDesc*>(e->maint_dev), rank, world,
+                                             buf + off);
+        if ((s = check_launch("k_scores_pack")) != TT_OK) return s;
+        off += msl;
+    }
+    return TT_OK;
+}
+
+tt_status tt_engine_sharded_scores_unpack(tt_engine* const* engines, int n, const float* buf, void* stream) {
+    if (n <= 0) return TT_OK;
+    if (!engines || !buf) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    for (int i = 0; i < n; ++i) {
+        tt_status s = validate(engines[i]);
+        if (s != TT_OK) return s;
+    }
+    DeviceGuard dg(engines[0]->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    size_t off = 0;
+    for (int i = 0; i < n; ++i) {
+        tt_engine* e = engines[i];
+        const size_t msl = (size_t)e->cfg.max_seq_len;
+        tt_status s = check_cuda(cudaMemcpyAsync(e->g, buf + off, msl * sizeof(float), cudaMemcpyDeviceToDevice, st),
+                                 "scores unpack");
+        if (s != TT_OK) return s;
+        k_scores_refresh_hh<<<std::max(1, ceil_div(e->max_hh, 256)), 256, 0, st>>>(
+            reinterpret_cast<const MaintDesc*>(e->maint_dev));
+        if ((s = check_launch("k_scores_refresh_hh")) != TT_OK) return s;
+        off += msl;
+    }
     return TT_OK;
 }
 
 tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const float* const* Q,
                                        const float* const* K_new, const float* const* V_new, int rank, int world,
-                                       int slot_cap, float* xch_send, void* stream) {
+                                       const void* route_all, float* xch_send, void* stream) {
     if (n <= 0) return TT_OK;
-    tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
+    tt_status s = validate_shard_args(engines, n, rank, world);
     if (s != TT_OK) return s;
     s = validate_step(engines, n, Q, K_new, V_new);
     if (s != TT_OK) return s;
     if (!xch_send) return set_error(TT_ERR_INVALID_ARGUMENT, "xch_send must not be NULL.");
-    for (int i = 0; i < n; ++i)
-        if (shard_slot_need(engines[i], world) > slot_cap)
-            return set_error(TT_ERR_INVALID_ARGUMENT,
-                             "slot_cap %d is below this step's need (tt_engine_sharded_slot_cap).", slot_cap);
+    if (route_all && ((uintptr_t)route_all & 15))
+        return set_error(TT_ERR_INVALID_ARGUMENT, "route_all must be 16-byte aligned.");
+    if (route_all && world > 1)
+        for (int i = 0; i < n; ++i)
+            if (step_recomputes_threshold(engines[i]))
+                return set_error(TT_ERR_INVALID_ARGUMENT,
+                                 "this step recomputes the heavy-hitter threshold: synchronise the scores "
+                                 "(tt_engine_sharded_scores_pack / _unpack) and pass route_all = NULL.");
     DeviceGuard dg(engines[0]->cfg.device);
     cudaStream_t st = (cudaStream_t)stream;
     int dcap = 0, pcap = 0;
-    s = maintain_batch(engines, n, K_new, V_new, st, dcap, pcap);
+    s = maintain_batch(engines, n, K_new, V_new, st, dcap, pcap, static_cast<const RouteRow*>(route_all), world);
     if (s != TT_OK) return s;
     AttnLaunch L;
     memset(&L, 0, sizeof(L));
     L.njobs = n;
     const tt_engine_config& c0 = engines[0]->cfg;
-    // this rank's share: ceil(D / world) dense positions, ceil(blocks / world) blocks
-    const int chunk = engines[0]->chunk;
-    const int pcap_r = ceil_div(ceil_div(pcap, chunk), world) * chunk;
-    s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, ceil_div(dcap, world), pcap_r);
+    int dcap_r = 0, pcap_r = 0;
+    for (int i = 0; i < n; ++i) {
+        int d = 0, p = 0;
+        shard_caps(engines[i], step_block_bound(engines[i]), world, d, p);
+        dcap_r = std::max(dcap_r, d);
+        pcap_r = std::max(pcap_r, p);
+    }
+    s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, dcap_r, pcap_r);
     if (s != TT_OK) return s;
+    // packed chunks cover whole ownership granules (a stage or a 32-token unit
+    // never crosses a granule)
+    L.PC = ceil_div(L.PC, kShardGran) * kShardGran;
+    L.np = ceil_div(pcap_r, L.PC);
     fill_launch(L, engines, n, Q, nullptr);
     L.rank = rank;
     L.world = world;
@@ -927,14 +1088,14 @@ tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const f
     return TT_OK;
 }
 
-tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
-                                       const float* xch_all, float* const* attn_output, float* mw_send,
-                                       void* stream) {
+tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int rank, int world, const float* xch_all,
+                                       float* const* attn_output, void* route_send, void* stream) {
     if (n <= 0) return TT_OK;
-    tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
+    tt_status s = validate_shard_args(engines, n, rank, world);
     if (s != TT_OK) return s;
-    if (!xch_all || !attn_output || !mw_send) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if (!xch_all || !attn_output || !route_send) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
     if ((uintptr_t)xch_all & 7) return set_error(TT_ERR_INVALID_ARGUMENT, "xch_all must be 8-byte aligned.");
+    if ((uintptr_t)route_send & 15) return set_error(TT_ERR_INVALID_ARGUMENT, "route_send must be 16-byte aligned.");
     for (int i = 0; i < n; ++i)
         if (!attn_output[i]) return set_error(TT_ERR_INVALID_ARGUMENT, "attn_output must not be NULL.");
     DeviceGuard dg(engines[0]->cfg.device);
@@ -943,22 +1104,13 @@ tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int ran
     fill_launch(L, engines, n, nullptr, attn_output);
     L.rank = rank;
     L.world = world;
-    return launch_sharded_merge(L, xch_all, mw_send, slot_cap, (cudaStream_t)stream);
-}
-
-tt_status tt_engine_step_sharded_end(tt_engine* const* engines, int n, int rank, int world, int slot_cap,
-                                     const float* mw_all, void* stream) {
-    if (n <= 0) return TT_OK;
-    tt_status s = validate_shard_args(engines, n, rank, world, slot_cap);
-    if (s != TT_OK) return s;
-    if (!mw_all) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
-    DeviceGuard dg(engines[0]->cfg.device);
-    AttnLaunch L;
-    memset(&L, 0, sizeof(L));
-    fill_launch(L, engines, n, nullptr, nullptr);
-    L.rank = rank;
-    L.world = world;
-    return launch_sharded_feedback(L, mw_all, slot_cap, (cudaStream_t)stream);
+    int pos_cap = 0;
+    for (int i = 0; i < n; ++i) {  // the mirrors already count the step begun
+        int d = 0, p = 0;
+        shard_caps(engines[i], engines[i]->h_wr_pbs_ub / engines[i]->chunk, world, d, p);
+        pos_cap = std::max(pos_cap, d + p);
+    }
+    return launch_sharded_merge(L, xch_all, static_cast<RouteRow*>(route_send), pos_cap, (cudaStream_t)stream);
 }
 
 tt_status tt_engine_step(tt_engine* e, const float* Q, const float* K_new, const float* V_new, float* attn_output,
@@ -1171,6 +1323,7 @@ tt_status tt_engine_set_counters(tt_engine* e, const tt_engine_counters* in, voi
     e->h_rw = c.rw_count;
     e->h_rw_head = c.rw_head_index;
     e->h_evictions = c.total_evictions;
+    e->h_last_calc = c.last_calc_pos;
     e->h_wr_pbs_ub = (long long)c.pbs_count + c.wr_count;
     e->last_stream = st;
     return TT_OK;

@@ -154,17 +154,12 @@ __host__ __device__ __forceinline__ size_t partial_smem_bytes(int HG, int mb) {
     return q + (body > merge ? body : merge);
 }
 
-__device__ __forceinline__ void dense_slot(const JobDesc& J, const TierCounts& tc, int i, const float*& Kb,
+// K/V tier rows and slot of local dense position i (tt_attn.cuh numbering).
+__device__ __forceinline__ void dense_slot(const JobDesc& J, const TierCounts& tc, int i, int r, int w, const float*& Kb,
                                            const float*& Vb, int& slot) {
-    if (i < tc.n0) {
-        Kb = J.K0; Vb = J.V0; slot = i;
-    } else if (i < tc.n0 + tc.n1) {
-        Kb = J.K1; Vb = J.V1; slot = i - tc.n0;
-    } else {
-        Kb = J.K2; Vb = J.V2;
-        const int r = i - tc.n0 - tc.n1;
-        slot = tc.ring_size > 0 ? (tc.ring_head + r) % tc.ring_size : r;
-    }
+    const int tier = dense_local_slot(tc, i, r, w, slot);
+    Kb = tier == 0 ? J.K0 : tier == 1 ? J.K1 : J.K2;
+    Vb = tier == 0 ? J.V0 : tier == 1 ? J.V1 : J.V2;
 }
 
 // Per-warp online-softmax state.  acc holds channel pairs (lane owns CPL channels).
@@ -264,11 +259,11 @@ __device__ __forceinline__ void load_wrow(const u64* wt, u64 (&w)[GM]) {
 template <int HD, int GM>
 __device__ __forceinline__ void pbs_issue_stage(const JobDesc& J, int HG, int hg, int t0, int t1, int s,
                                                 unsigned char* stages, const StageLayout& SL, uint64_t* bars,
-                                                int lane) {
+                                                int lane, int rank, int world) {
     constexpr int DQ = HDT<HD>::DQ;
     const int ST = stage_tokens(HG);
-    const int s0 = t0 + s * ST;
-    const int nt = min(ST, t1 - s0);
+    const int nt = min(ST, t1 - (t0 + s * ST));
+    const int s0 = packed_global(t0 + s * ST, rank, world);  // a stage lies inside one ownership granule
     const int grp = J.grp, nkv = J.nkv, h0 = hg * HG;
     // Every copy below starts 16-byte aligned and moves a multiple of 16 bytes:
     // HG == nkv gives one contiguous run per region; otherwise HG == 8 and the
@@ -586,10 +581,11 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
     const int hg = by - job * L.nhg;
     const int D = tc.n0 + tc.n1 + tc.n2;
     // this launch's share of the positions (all of them unless sharded)
-    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
-    const int t0 = R.plo + bx * L.PC;
-    const int t1 = min(R.phi, t0 + L.PC);
+    const ShardMap M = shard_map(tc, J.grp, L.rank, L.world);
+    const int t0 = bx * L.PC;  // local packed tokens [t0, t1): sharded launches use PC % kShardGran == 0,
+    const int t1 = min(M.np, t0 + L.PC);  // so stages and units never cross an ownership granule
     if (t0 >= t1) return;
+    const int Dl = M.nd;  // local dense positions precede the local packed ones in the logits
 
     const int G = L.G, HG = L.HG;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -616,7 +612,7 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
         __syncthreads();
         if (warp == 0)
             for (int s = 0; s < NS && s < nst; ++s)
-                pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s, stages, SL, bars, lane);
+                pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s, stages, SL, bars, lane, L.rank, L.world);
     }
 
     // ---- query rows of this kv-head group: q_s[kvl][g][c] ----
@@ -630,7 +626,7 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
     const float* qk = q_s + (size_t)kvl * GM * HD;
     // partial slot: this job's active chunks, dense first, packed after (compact,
     // so a job's slots never depend on the other jobs of a batch)
-    const int chunk = ceil_div(R.dhi - R.dlo, L.DC) + bx;
+    const int chunk = ceil_div(M.nd, L.DC) + bx;
     float* mbuf = reinterpret_cast<float*>(smem + qbytes);  // merge buffer (aliases the stages / warp areas)
 
     if (MMA) {
@@ -660,8 +656,8 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
                 mma_prepare_q<HD, GMv>(qv, lane, sc, wa, Qf);
                 auto issue = [&](int k) {
                     const int s0 = t0 + (r0v + k * WPHv) * 32;
-                    mma_issue<HD>(J, kvh_r, s0, min(32, t1 - s0), wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes,
-                                  lane);
+                    mma_issue<HD>(J, kvh_r, packed_global(s0, L.rank, L.world), min(32, t1 - s0),
+                                  wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, lane);
                 };
 #pragma unroll
                 for (int k = 0; k < kMmaSlots - 1; ++k) {
@@ -675,7 +671,7 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
                     cp_async_wait<kMmaSlots - 1>();  // unit k's copies (this lane's) have landed
                     __syncwarp();                    // ... and every lane's are visible
                     const int s0 = t0 + (r0v + k * WPHv) * 32;
-                    pbs_unit_mma<HD, GMv>(J, hbase, gcnt, kvh_r, lane, D,
+                    pbs_unit_mma<HD, GMv>(J, hbase, gcnt, kvh_r, lane, Dl,
                                           wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, s0, min(32, t1 - s0), Qf,
                                           wa, S);
                 }
@@ -734,9 +730,9 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
             const unsigned char* buf = stages + (size_t)(s % NSTAGE) * SL.bytes;
             const int s0 = t0 + s * ST;
             const int nt = min(ST, t1 - s0);
-            if (active && r0 * 32 < nt) pbs_unit<HD, GM>(J, HG, G, kvl, kvh, lane, D, buf, SL, s0, nt, r0, qk, wa, sc, S);
+            if (active && r0 * 32 < nt) pbs_unit<HD, GM>(J, HG, G, kvl, kvh, lane, Dl, buf, SL, s0, nt, r0, qk, wa, sc, S);
             __syncthreads();
-            if (warp == 0 && s + NSTAGE < nst) pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s + NSTAGE, stages, SL, bars, lane);
+            if (warp == 0 && s + NSTAGE < nst) pbs_issue_stage<HD, GM>(J, HG, hg, t0, t1, s + NSTAGE, stages, SL, bars, lane, L.rank, L.world);
         }
         if (failed) {
             // drain this CTA's own copies in flight, then give up on the chunk
@@ -841,9 +837,8 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
     __syncthreads();
     if (!last) return;
     const int nq = J.nq;
-    const int D = tc.n0 + tc.n1 + tc.n2;
-    const ShardRange R = shard_range(D, tc.nblk, J.grp, L.rank, L.world);
-    const int nch = ceil_div(R.dhi - R.dlo, L.DC) + ceil_div(R.phi - R.plo, L.PC);
+    const ShardMap M = shard_map(tc, J.grp, L.rank, L.world);
+    const int nch = ceil_div(M.nd, L.DC) + ceil_div(M.np, L.PC);
     const int tq = threadIdx.x % TPH;
     const float2* pml = reinterpret_cast<const float2*>(J.part_ml);
     for (int h = threadIdx.x / TPH; h < nq; h += HPP) {  // the TPH threads of a head are adjacent lanes
@@ -884,6 +879,7 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
                 xr[0] = M;
                 xr[1] = S;
             }
+            if (threadIdx.x == 0 && h == 0) *route_min_word(J) = 0ull;
         } else {
             const float inv = 1.0f / (S > 0.f ? S : 1.0f);
             float* out = L.out[job] + (size_t)h * HD;

@@ -18,6 +18,14 @@ __device__ __forceinline__ float* head_ml(const JobDesc& J) {
     return J.part_ml + (size_t)(J.max_chunks - 1) * J.nq * 2;
 }
 
+// Smallest (score, heavy-hitter slot) of a sequence-sharded merge launch, as
+// the complement of order_key(score) << 32 | slot so that zero means "none"
+// and atomicMax finds the minimum.  It lives in the job's head (M, 1/L) slot,
+// which sharded steps do not use otherwise; their partial launch zeroes it.
+__device__ __forceinline__ unsigned long long* route_min_word(const JobDesc& J) {
+    return reinterpret_cast<unsigned long long*>(head_ml(J));
+}
+
 // Weight of position pos averaged over heads: (1/nq) sum_h 2^(s_h - M_h) / L_h,
 // skipping -inf logits (fused_attn_avx2.cpp:286-300).  The logits come
 // through L2: in the partial kernel other CTAs wrote them during the launch.
@@ -52,6 +60,25 @@ __device__ __forceinline__ long long position_id(const JobDesc& J, const TierCou
     }
     if (pos < D) return (long long)tc.total - tc.n2 + (pos - tc.n0 - tc.n1);
     return J.ids[pos - D];
+}
+
+// Token id at local position i of a sequence-sharded rank's share (its dense
+// positions, then its packed tokens; world <= 1: the global position) and,
+// for heavy hitters, the HH slot; -1 where there is none.
+__device__ __forceinline__ long long local_position_id(const JobDesc& J, const TierCounts& tc, const ShardMap& M,
+                                                       int r, int w, int i, int& hh) {
+    hh = -1;
+    if (i < M.nd) {
+        int slot;
+        const int tier = dense_local_slot(tc, i, r, w, slot);
+        if (tier == 0) return slot;
+        if (tier == 1) {
+            hh = slot;
+            return J.hh_ids[slot];
+        }
+        return ring_slot_id(tc, slot);
+    }
+    return J.ids[packed_global(i - M.nd, r, w)];
 }
 
 // The mean weight of position pos (written to mw when given) and, for
