@@ -7,7 +7,8 @@
 // pairs with 1-D TMA bulk copies (cp.async.bulk ... mbarrier::complete_tx),
 // two stages in flight.  Every mbarrier wait is bounded: on expiry the CTA
 // records TT_ERR_TIMEOUT in the device error word, drains its own copies
-// (again bounded) and returns.  No multicast and no cluster launch.
+// (again bounded) and returns.  Every copy lands in the issuing CTA's own
+// shared memory; no cluster launch.
 //
 // Per 32-token unit and kv head (one warp):
 //   QK lane <-> token:  score = sum_c qs_c*(4+code) - 4*sum qs + sum q*zero,
@@ -102,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase)
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
-// 1-D bulk copy global -> shared, completion counted on `bar` (no multicast).
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
 __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_addr(dst)),
