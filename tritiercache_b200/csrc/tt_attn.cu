@@ -143,8 +143,11 @@ __global__ void __launch_bounds__(NT) k_attn_merge_heads(const __grid_constant__
 }
 
 // Mean attention weights over heads (fused_attn_avx2.cpp:286-300) and, for
-// engines, the score feedback; one position per thread, CTAs stride over the
-// job's positions.  grid (gx, njobs); dynamic shared memory: 2 nq floats.
+// engines, the score feedback.  Four consecutive positions per thread (float4
+// logit rows; the token ids and old scores are loaded first, so their latency
+// overlaps the logit loads), CTAs striding over the job's positions; one
+// position per thread where the logit rows are not 16-byte aligned.
+// grid (gx, njobs); dynamic shared memory: 2 nq floats.
 __global__ void __launch_bounds__(NT, 4) k_attn_weights(const __grid_constant__ AttnLaunch L) {
     extern __shared__ float fsm[];
     __shared__ JobDesc Js;
@@ -160,15 +163,48 @@ __global__ void __launch_bounds__(NT, 4) k_attn_weights(const __grid_constant__ 
     if (threadIdx.x == 0) Ts = resolve_counts(J);
     const float* ml = head_ml(J);
     for (int h = threadIdx.x; h < nq; h += NT) {
-        Ms[h] = ml[2 * h];
+        const float m = ml[2 * h];
+        Ms[h] = m == -INFINITY ? INFINITY : m;  // a head without logits: every term 2^-inf = 0
         IL[h] = ml[2 * h + 1];
     }
     __syncthreads();
     const TierCounts tc = Ts;
     const int D = tc.n0 + tc.n1 + tc.n2;
     const int T = D + tc.nblk * J.grp;
-    for (int pos = blockIdx.x * NT + threadIdx.x; pos < T; pos += gridDim.x * NT)
-        weigh_position(J, tc, D, Ms, IL, L.mw[job], pos);
+    float* mw = L.mw[job];
+    const bool vec = ((reinterpret_cast<uintptr_t>(J.scores) & 15) == 0) && (J.score_stride & 3) == 0;
+    if (!vec) {
+        for (int pos = blockIdx.x * NT + threadIdx.x; pos < T; pos += gridDim.x * NT)
+            weigh_position(J, tc, D, Ms, IL, mw, pos);
+        return;
+    }
+    for (int p4 = (blockIdx.x * NT + threadIdx.x) * 4; p4 < T; p4 += gridDim.x * NT * 4) {
+        long long id[4];
+        int hh[4];
+        float g0[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            hh[k] = -1;
+            id[k] = (J.g && p4 + k < T) ? position_id(J, tc, D, p4 + k, hh[k]) : -1;
+            if (id[k] >= J.msl) id[k] = -1;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) g0[k] = id[k] >= 0 ? J.g[id[k]] : 0.f;
+        const float4 w4 = mean_weight4(J, Ms, IL, nq, p4);  // rows are stride >= T + 3 floats long
+        const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+        if (mw) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (p4 + k < T) mw[p4 + k] = w[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {  // positions hold distinct tokens: no two updates meet
+            if (id[k] < 0) continue;
+            const float nv = fmaf(J.decay, g0[k], w[k]);
+            J.g[id[k]] = nv;
+            if (hh[k] >= 0) J.hh_scores[hh[k]] = nv;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -311,25 +347,47 @@ __global__ void __launch_bounds__(NT) k_shard_merge(const __grid_constant__ Attn
             out[(size_t)h * HD + c] = o;
         }
     }
+    __syncthreads();  // every thread has read Ms before the substitution below
+    for (int h = threadIdx.x; h < nq; h += NT)
+        if (Ms[h] == -INFINITY) Ms[h] = INFINITY;  // a head without logits: every term 2^-inf = 0
+    __syncthreads();
     // feedback of this rank's positions; the heavy-hitter minimum over them
     const int r = L.rank;
     const ShardMap SM = shard_map(tc, J.grp, r, P);
     const int n_loc = SM.nd + SM.np;
     unsigned long long best = 0ull;  // complemented key, 0 = none
+    const bool vec = ((reinterpret_cast<uintptr_t>(J.scores) & 15) == 0) && (J.score_stride & 3) == 0;
     if (J.g) {
-        for (int i = blockIdx.x * NT + threadIdx.x; i < n_loc; i += gridDim.x * NT) {
-            int hh;
-            long long id = local_position_id(J, tc, SM, r, P, i, hh);
-            const bool fb = id >= 0 && id < J.msl;
-            const float g_old = fb ? J.g[id] : 0.f;
-            const float w = mean_weight(J, Ms, IL, nq, i);
-            if (!fb) continue;
-            const float nv = fmaf(J.decay, g_old, w);
-            J.g[id] = nv;
-            if (hh >= 0) {
-                J.hh_scores[hh] = nv;
-                const unsigned long long key = ~(((unsigned long long)order_key(nv) << 32) | (uint32_t)hh);
-                best = key > best ? key : best;
+        const int per = vec ? 4 : 1;  // positions per thread: float4 logit rows where aligned
+        for (int i0 = (blockIdx.x * NT + threadIdx.x) * per; i0 < n_loc; i0 += gridDim.x * NT * per) {
+            long long id[4];
+            int hh[4];
+            float g0[4], w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                hh[k] = -1;
+                id[k] = (k < per && i0 + k < n_loc) ? local_position_id(J, tc, SM, r, P, i0 + k, hh[k]) : -1;
+                if (id[k] >= J.msl) id[k] = -1;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) g0[k] = id[k] >= 0 ? J.g[id[k]] : 0.f;
+            if (vec) {
+                const float4 w4 = mean_weight4(J, Ms, IL, nq, i0);
+                w[0] = w4.x; w[1] = w4.y; w[2] = w4.z; w[3] = w4.w;
+            } else {
+                w[0] = mean_weight(J, Ms, IL, nq, i0);
+                w[1] = w[2] = w[3] = 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                if (id[k] < 0) continue;
+                const float nv = fmaf(J.decay, g0[k], w[k]);
+                J.g[id[k]] = nv;
+                if (hh[k] >= 0) {
+                    J.hh_scores[hh[k]] = nv;
+                    const unsigned long long key = ~(((unsigned long long)order_key(nv) << 32) | (uint32_t)hh[k]);
+                    best = key > best ? key : best;
+                }
             }
         }
     }
@@ -568,7 +626,7 @@ tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t s
 tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, RouteRow* route, int pos_cap,
                                cudaStream_t st) {
     // about 8 CTAs per SM over the launch for the feedback, at least one per head
-    const int gx = std::max(L.inline_job.nq, std::min(ceil_div(std::max(pos_cap, 1), NT), std::max(1, 8 * 148 / L.njobs)));
+    const int gx = std::max(L.inline_job.nq, std::min(ceil_div(std::max(pos_cap, 1), 4 * NT), std::max(1, 8 * 148 / L.njobs)));
     dim3 grid(gx, L.njobs);
     const int ps = prof_begin(2, st);
     k_shard_merge<<<grid, NT, (size_t)2 * L.inline_job.nq * sizeof(float), st>>>(L, xch_all, route);
@@ -608,7 +666,7 @@ tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
     // SM over the launch (several waves of short CTAs: each thread's chain of
     // dependent loads is short), each striding over its job's positions
     const long long tcap = (long long)L.nd * L.DC + (long long)L.np * L.PC;
-    const long long gx = std::min<long long>((tcap + NT - 1) / NT, std::max(1, 8 * 148 / L.njobs));
+    const long long gx = std::min<long long>((tcap + 4 * NT - 1) / (4 * NT), std::max(1, 8 * 148 / L.njobs));
     dim3 grid((unsigned)std::max<long long>(1, gx), L.njobs);
     const int ps = prof_begin(2, st);
     k_attn_weights<<<grid, NT, (size_t)2 * nq * sizeof(float), st>>>(L);
@@ -701,8 +759,9 @@ extern "C" tt_status tt_fused_attention_decode(const float* Q, const float* dens
     if (s != TT_OK) return s;
     const int T = dense_count + ntok;
     const int maxch = L.nd + L.np;
-    const size_t stride = (size_t)std::max(T, 1);
-    const size_t need = (size_t)maxch * num_q_heads * (head_dim + 2) + (size_t)num_q_heads * stride + 64;
+    const size_t stride = ((size_t)std::max(T, 1) + 3) / 4 * 4;  // float4 logit rows
+    const size_t ml_floats = ((size_t)maxch * num_q_heads * 2 + 3) / 4 * 4;
+    const size_t need = ml_floats + (size_t)maxch * num_q_heads * head_dim + (size_t)num_q_heads * stride + 64;
     float* ws = nullptr;
     s = workspace(dev, need, &ws);
     if (s != TT_OK) return s;
@@ -715,7 +774,7 @@ extern "C" tt_status tt_fused_attention_decode(const float* Q, const float* dens
     J.vp = PBS_V_Packed; J.vs = PBS_V_Scales; J.vz = PBS_V_Zeroes; J.ids = PBS_token_ids;
     J.ctr = nullptr;
     J.part_ml = ws;
-    J.part_acc = ws + (size_t)maxch * num_q_heads * 2;
+    J.part_acc = ws + ml_floats;
     J.scores = J.part_acc + (size_t)maxch * num_q_heads * head_dim;
     J.score_stride = (int)stride;
     J.max_chunks = maxch;

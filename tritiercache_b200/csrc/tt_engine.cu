@@ -637,7 +637,7 @@ tt_status write_descriptors(tt_engine* e) {
     j.ctr = e->ctr;
     const int maxch = attn_max_chunks(dense_cap(e), e->pbs_cap * e->chunk);
     j.max_chunks = maxch;
-    j.score_stride = dense_cap(e) + e->pbs_cap * e->chunk;
+    j.score_stride = (dense_cap(e) + e->pbs_cap * e->chunk + 3) / 4 * 4;  // float4 logit rows
     j.part_ml = e->scratch;
     j.part_acc = e->scratch + ((size_t)maxch * j.nq * 2 + 3) / 4 * 4;  // 16-byte aligned (float4 reads)
     j.scores = j.part_acc + (size_t)maxch * j.nq * j.hd;
@@ -650,7 +650,7 @@ tt_status write_descriptors(tt_engine* e) {
 
 size_t scratch_need(const tt_engine* e, int pbs_cap) {
     const int maxch = attn_max_chunks(dense_cap(e), pbs_cap * e->chunk);
-    const size_t stride = (size_t)dense_cap(e) + (size_t)pbs_cap * e->chunk;
+    const size_t stride = ((size_t)dense_cap(e) + (size_t)pbs_cap * e->chunk + 3) / 4 * 4;
     return (size_t)maxch * e->cfg.num_q_heads * (e->cfg.head_dim + 2) + (size_t)e->cfg.num_q_heads * stride + 64;
 }
 

@@ -97,8 +97,9 @@ extern "C" tt_status tt_fused_attention_decode_noalloc(
     // [nq][T] logits -- the same layout the allocating entry point uses
     const int T = dense_count + ntok;
     const int maxch = L.nd + L.np;
-    const size_t stride = (size_t)(T > 0 ? T : 1);
-    const size_t need = (size_t)maxch * num_q_heads * (head_dim + 2) + (size_t)num_q_heads * stride + 64;
+    const size_t stride = ((size_t)(T > 0 ? T : 1) + 3) / 4 * 4;  // float4 logit rows
+    const size_t ml_floats = ((size_t)maxch * num_q_heads * 2 + 3) / 4 * 4;
+    const size_t need = ml_floats + (size_t)maxch * num_q_heads * head_dim + (size_t)num_q_heads * stride + 64;
     if (need * sizeof(float) > kNoAllocScratchBytes)
         return set_error(TT_ERR_INVALID_ARGUMENT,
                          "tt_fused_attention_decode_noalloc: this call needs %zu bytes of scratch but the fixed "
@@ -120,7 +121,7 @@ extern "C" tt_status tt_fused_attention_decode_noalloc(
     J.vp = PBS_V_Packed; J.vs = PBS_V_Scales; J.vz = PBS_V_Zeroes; J.ids = PBS_token_ids;
     J.ctr = nullptr;
     J.part_ml = ws;
-    J.part_acc = ws + (size_t)maxch * num_q_heads * 2;
+    J.part_acc = ws + ml_floats;
     J.scores = J.part_acc + (size_t)maxch * num_q_heads * head_dim;
     J.score_stride = (int)stride;
     J.max_chunks = maxch;

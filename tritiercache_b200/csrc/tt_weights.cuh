@@ -49,6 +49,41 @@ __device__ __forceinline__ float mean_weight(const JobDesc& J, const float* Ms, 
     return sw / (float)nq;
 }
 
+// Head-mean weights of the 4 positions p4 .. p4 + 3 (float4 logit loads; the
+// rows must be 16-byte aligned: J.scores and the stride a multiple of 4
+// floats).  Ms[h] is the head's max with -inf replaced by +inf (then every
+// logit of the head gives 2^-inf = 0, as the scalar form's skip of -inf
+// logits does), so the terms and their order match mean_weight exactly.
+__device__ __forceinline__ float4 mean_weight4(const JobDesc& J, const float* Ms, const float* IL, int nq, int p4) {
+    const float* sc = J.scores + p4;
+    const size_t stride = (size_t)J.score_stride;
+    float4 sw = make_float4(0.f, 0.f, 0.f, 0.f);
+    int h = 0;
+    for (; h + 8 <= nq; h += 8) {  // 8 rows in flight before the first use
+        float4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __ldcg(reinterpret_cast<const float4*>(sc + (size_t)(h + k) * stride));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float m = Ms[h + k], il = IL[h + k];
+            sw.x = fmaf(ex2_fast(v[k].x - m), il, sw.x);
+            sw.y = fmaf(ex2_fast(v[k].y - m), il, sw.y);
+            sw.z = fmaf(ex2_fast(v[k].z - m), il, sw.z);
+            sw.w = fmaf(ex2_fast(v[k].w - m), il, sw.w);
+        }
+    }
+    for (; h < nq; ++h) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(sc + (size_t)h * stride));
+        const float m = Ms[h], il = IL[h];
+        sw.x = fmaf(ex2_fast(v.x - m), il, sw.x);
+        sw.y = fmaf(ex2_fast(v.y - m), il, sw.y);
+        sw.z = fmaf(ex2_fast(v.z - m), il, sw.z);
+        sw.w = fmaf(ex2_fast(v.w - m), il, sw.w);
+    }
+    const float inv = (float)nq;
+    return make_float4(sw.x / inv, sw.y / inv, sw.z / inv, sw.w / inv);
+}
+
 // Token id at position pos (-1 where there is none) and, for heavy hitters,
 // the HH slot: sinks, heavy hitters, the recent ring, the packed tier.
 __device__ __forceinline__ long long position_id(const JobDesc& J, const TierCounts& tc, int D, int pos, int& hh) {
