@@ -655,28 +655,34 @@ __device__ __forceinline__ void packed_body(const AttnLaunch& L, const JobDesc& 
             const int nu = act && r0v < nu_all ? ceil_div(nu_all - r0v, WPHv) : 0;
             if (nu > 0) {
                 mma_prepare_q<HD, GMv>(qv, lane, sc, wa, Qf);
-                auto issue = [&](int k) {
-                    const int s0 = t0 + (r0v + k * WPHv) * 32;
-                    mma_issue<HD>(J, kvh_r, packed_global(s0, L.rank, L.world), min(32, t1 - s0),
-                                  wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, lane);
-                };
+                // the block size is a template parameter of the unit (16 or 32 tokens)
+                auto run = [&](auto gsh_tag) {
+                    constexpr int GSH = decltype(gsh_tag)::value;
+                    auto issue = [&](int k) {
+                        const int s0 = t0 + (r0v + k * WPHv) * 32;
+                        mma_issue<HD, GSH>(J, kvh_r, packed_global(s0, L.rank, L.world), min(32, t1 - s0),
+                                           wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, lane);
+                    };
 #pragma unroll
-                for (int k = 0; k < kMmaSlots - 1; ++k) {
-                    if (k < nu) issue(k);
-                    cp_async_commit();
-                }
-                for (int k = 0; k < nu; ++k) {
-                    // refill the slot unit k-1 used (released at the end of its iteration)
-                    if (k + kMmaSlots - 1 < nu) issue(k + kMmaSlots - 1);
-                    cp_async_commit();
-                    cp_async_wait<kMmaSlots - 1>();  // unit k's copies (this lane's) have landed
-                    __syncwarp();                    // ... and every lane's are visible
-                    const int s0 = t0 + (r0v + k * WPHv) * 32;
-                    pbs_unit_mma<HD, GMv>(J, hbase, gcnt, kvh_r, lane, Dl,
-                                          wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, s0, min(32, t1 - s0), Qf,
-                                          wa, S);
-                }
-                cp_async_wait<0>();
+                    for (int k = 0; k < kMmaSlots - 1; ++k) {
+                        if (k < nu) issue(k);
+                        cp_async_commit();
+                    }
+                    for (int k = 0; k < nu; ++k) {
+                        // refill the slot unit k-1 used (released at the end of its iteration)
+                        if (k + kMmaSlots - 1 < nu) issue(k + kMmaSlots - 1);
+                        cp_async_commit();
+                        cp_async_wait<kMmaSlots - 1>();  // unit k's copies (this lane's) have landed
+                        __syncwarp();                    // ... and every lane's are visible
+                        const int s0 = t0 + (r0v + k * WPHv) * 32;
+                        pbs_unit_mma<HD, GMv, GSH>(J, hbase, gcnt, kvh_r, lane, Dl,
+                                                   wa + (size_t)(k % kMmaSlots) * MmaStage<HD>::bytes, s0,
+                                                   min(32, t1 - s0), Qf, wa, S);
+                    }
+                    cp_async_wait<0>();
+                };
+                if (J.grp == 32) run(std::integral_constant<int, 5>{});
+                else run(std::integral_constant<int, 4>{});
             }
             float m, l, o[HD / 16][2];
             mma_finish<HD>(S, m, l, o);

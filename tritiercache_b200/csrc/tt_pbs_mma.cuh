@@ -204,12 +204,12 @@ struct MmaState {
 // kvh into stage st with per-lane cp.async; the caller commits the group.
 // Every source offset is a multiple of 16 bytes (4 for the V scale/zero pairs:
 // the number of kv heads is even), every size a multiple of the copy size.
-template <int HD>
+template <int HD, int GSH>
 __device__ __forceinline__ void mma_issue(const JobDesc& J, int kvh, int s0, int nt, unsigned char* st, int lane) {
     using SL = MmaStage<HD>;
     constexpr int DQ = HD / 16;
     const int nkv = J.nkv;
-    const int gsh = J.grp == 32 ? 5 : 4;
+    constexpr int gsh = GSH;  // log2 of the block size (16 or 32)
     // per-array bases of this unit (uniform across the warp) + 32-bit lane offsets
     const char* kb = reinterpret_cast<const char*>(J.kp) + ((size_t)(s0 >> 4) * nkv + kvh) * (HD * 4);
     const size_t moff = ((size_t)(s0 >> gsh) * nkv + kvh) * (HD * 2);
@@ -284,9 +284,10 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x (PTX ex2.approx; 
 }
 
 // One 32-token unit [s0, s0 + nt) of kv head kvh from stage st.
-template <int HD, int GM>
+template <int HD, int GM, int GSH>
 // hbase / gcnt: the first of this warp's query heads and how many there are
-// (<= 4); kvh: the kv head whose packed bytes the unit reads.
+// (<= 4); kvh: the kv head whose packed bytes the unit reads; GSH: log2 of the
+// block size (4: 16 tokens, 5: 32 tokens).
 __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int hbase, int gcnt, int kvh, int lane, int D,
                                              const unsigned char* st, int s0, int nt, const MmaQ<HD>& Q,
                                              unsigned char* wa, MmaState<HD>& S) {
@@ -298,7 +299,7 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int hbase, int gc
     const uint32_t m8 = 1u << (8 - sft);
     const uint32_t sel = 0x6420u + 0x1111u * (uint32_t)(gid >> 2);
     __half* wtab = reinterpret_cast<__half*>(wa + MmaWarpArea<HD>::wtab);
-    const int gsh = J.grp == 32 ? 5 : 4;  // log2 of the block size (16 or 32)
+    constexpr int gsh = GSH;
     const uint32_t* kw_s = reinterpret_cast<const uint32_t*>(st + SL::kw);
     const __half* ks_s = reinterpret_cast<const __half*>(st + SL::ks);
     const __half* kz_s = reinterpret_cast<const __half*>(st + SL::kz);
@@ -321,12 +322,14 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int hbase, int gc
         // (sv0 / sv1 below); their zeros come with one 8-byte load
         const int mo = ((16 * (gid & 1)) >> gsh) * HD + 4 * tig;
         const __half* mz_row = kz_s + mo;
-        const bool odd_blk = (gid & 1) != 0 && gsh == 4;
+        constexpr bool shared_blk = gsh == 5;  // both halves in one block: same B fragments
         const uint32_t* kw0 = kw_s + 4 * tig;
         const uint32_t* kw1 = kw0 + HD;
         const __half* sb0 = ks_s + 4 * tig;
         const __half* sb1 = ks_s + (16 >> gsh) * HD + 4 * tig;
-        const bool shared_blk = gsh == 5;  // both halves in one block: same B fragments
+        // bias rows of half gid&1: that block's scales (one more 8-byte load per
+        // k-step instead of two selects)
+        const __half* sbb = (!shared_blk && (gid & 1)) ? sb1 : sb0;
         const uint32_t* qm_t = reinterpret_cast<const uint32_t*>(wa + MmaWarpArea<HD>::qtab) +
                                ((gid & 1) ? (gid >> 1) * 4 + tig : 16 + tig) * 2;
 #pragma unroll
@@ -337,13 +340,13 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int hbase, int gc
             const uint2 zv = *reinterpret_cast<const uint2*>(mz_row + 16 * ks);
             const uint2 qm = *reinterpret_cast<const uint2*>(qm_t + ks * 40);
             uint2 sv1 = sv0;
-            if (!shared_blk) sv1 = *reinterpret_cast<const uint2*>(sb1 + 16 * ks);
-            const uint2 svb = odd_blk ? sv1 : sv0;
+            if constexpr (!shared_blk) sv1 = *reinterpret_cast<const uint2*>(sb1 + 16 * ks);
+            const uint2 svb = *reinterpret_cast<const uint2*>(sbb + 16 * ks);
             mma_f16_16816(bd, svb.x, zv.x, svb.y, zv.y, Q.qx[ks][0], Q.qx[ks][1]);
             const uint32_t b00 = b_qs(qm.x, Q.qx[ks][0], sv0.x);
             const uint32_t b01 = b_qs(qm.y, Q.qx[ks][1], sv0.y);
             uint32_t b10 = b00, b11 = b01;
-            if (!shared_blk) {
+            if constexpr (!shared_blk) {
                 b10 = b_qs(qm.x, Q.qx[ks][0], sv1.x);
                 b11 = b_qs(qm.y, Q.qx[ks][1], sv1.y);
             }
