@@ -506,6 +506,9 @@ class TriTierCacheEngine:
         self._keep = (w, idt)
 
 
+_row_arrays: dict = {}  # pointer arrays of 2-D row tensors, by (address, row bytes, rows)
+
+
 def _ptr_array(ts, n: int, name: str):
     """ctypes array of n device pointers: `ts` is a sequence of contiguous
     CUDA tensors, or one 2-D CUDA tensor whose n rows (each contiguous, any
@@ -516,8 +519,15 @@ def _ptr_array(ts, n: int, name: str):
         if not (ts.is_cuda and ts.dim() == 2 and ts.shape[0] == n and (ts.stride(1) == 1 or ts.shape[1] == 1)):
             raise ValueError(f"{name}: expected a 2-D CUDA tensor with {n} contiguous rows.")
         row = ts.stride(0) * ts.element_size()
-        p = np.arange(n, dtype=np.uint64) * np.uint64(row) + np.uint64(ts.data_ptr())
-        return arr.from_buffer_copy(p.tobytes())
+        key = (ts.data_ptr(), row, n)  # the array is a function of these alone
+        a = _row_arrays.get(key)
+        if a is None:
+            p = np.arange(n, dtype=np.uint64) * np.uint64(row) + np.uint64(ts.data_ptr())
+            a = arr.from_buffer_copy(p.tobytes())
+            if len(_row_arrays) > 256:
+                _row_arrays.clear()
+            _row_arrays[key] = a
+        return a
     if len(ts) != n:
         raise ValueError(f"{name}: expected {n} entries, got {len(ts)}.")
     out = []

@@ -533,13 +533,23 @@ __global__ void k_accumulate_scores(float* __restrict__ g, int msl, const float*
 // ---------------------------------------------------------------------------
 // score synchronisation of sequence-sharded steps
 // ---------------------------------------------------------------------------
+// Engines of one synchronisation and the offset of each one's scores in the
+// exchanged buffer ([sum of max_seq_len] floats, engine after engine).
+struct ScoreBatch {
+    int n;
+    const MaintDesc* d[kMaxBatch];
+    long long off[kMaxBatch];
+};
+
 // buf[id] = g[id] for the tokens rank `r` of `w` owns (zero elsewhere; the
 // caller zeroes buf): its sink, heavy-hitter and ring slots (slot % w == r),
 // its packed granules, and on rank 0 the waiting room, whose scores every
 // rank holds.  Summed over the ranks, buf is every token's current score.
-__global__ void __launch_bounds__(256) k_scores_pack(const MaintDesc* __restrict__ Ed, int r, int w,
-                                                     float* __restrict__ buf) {
-    const MaintDesc& E = *Ed;
+// grid (gx, engines).
+__global__ void __launch_bounds__(256) k_scores_pack(const __grid_constant__ ScoreBatch B, int r, int w,
+                                                     float* __restrict__ buf_all) {
+    const MaintDesc& E = *B.d[blockIdx.y];
+    float* buf = buf_all + B.off[blockIdx.y];
     const DevCounters c = *E.ctr;
     TierCounts tc;
     tc.n0 = c.s_count; tc.n1 = c.hh_count; tc.n2 = c.rw_count; tc.ring_head = c.rw_head; tc.ring_size = E.R;
@@ -569,13 +579,19 @@ __global__ void __launch_bounds__(256) k_scores_pack(const MaintDesc* __restrict
     }
 }
 
-// HH_scores[i] = g[HH_ids[i]]: the heavy hitters' copy of the synchronised scores.
-__global__ void k_scores_refresh_hh(const MaintDesc* __restrict__ Ed) {
-    const MaintDesc& E = *Ed;
-    const int n = E.ctr->hh_count;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+// g = buf and HH_scores[i] = buf[HH_ids[i]] (the heavy hitters' copy of the
+// synchronised scores).  grid (gx, engines).
+__global__ void __launch_bounds__(256) k_scores_unpack(const __grid_constant__ ScoreBatch B,
+                                                       const float* __restrict__ buf_all) {
+    const MaintDesc& E = *B.d[blockIdx.y];
+    const float* buf = buf_all + B.off[blockIdx.y];
+    const int nh = E.ctr->hh_count;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < E.msl;
+         i += (long long)gridDim.x * blockDim.x)
+        E.g[i] = buf[i];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nh; i += gridDim.x * blockDim.x) {
         const long long id = E.HH_ids[i];
-        if (id >= 0 && id < E.msl) E.HH_scores[i] = E.g[id];
+        if (id >= 0 && id < E.msl) E.HH_scores[i] = buf[id];
     }
 }
 
@@ -1000,43 +1016,46 @@ tt_status tt_engine_sharded_scores_pack(tt_engine* const* engines, int n, int ra
     if (!buf) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
     DeviceGuard dg(engines[0]->cfg.device);
     cudaStream_t st = (cudaStream_t)stream;
-    size_t off = 0;
+    ScoreBatch B;
+    memset(&B, 0, sizeof(B));
+    B.n = n;
+    long long off = 0, items = 1;
     for (int i = 0; i < n; ++i) {
         tt_engine* e = engines[i];
-        const size_t msl = (size_t)e->cfg.max_seq_len;
-        if ((s = check_cuda(cudaMemsetAsync(buf + off, 0, msl * sizeof(float), st), "scores pack")) != TT_OK) return s;
-        const long long items = (long long)dense_cap(e) + e->chunk + (long long)e->pbs_cap * e->chunk;
-        const int grid = (int)std::min<long long>((items + 255) / 256, 4 * 148);
-        k_scores_pack<<<grid, 256, 0, st>>>(reinterpret_cast<const MaintDesc*>(e->maint_dev), rank, world,
-                                             buf + off);
-        if ((s = check_launch("k_scores_pack")) != TT_OK) return s;
-        off += msl;
+        B.d[i] = reinterpret_cast<const MaintDesc*>(e->maint_dev);
+        B.off[i] = off;
+        off += e->cfg.max_seq_len;
+        items = std::max<long long>(items, (long long)dense_cap(e) + e->chunk + (long long)e->pbs_cap * e->chunk);
     }
-    return TT_OK;
+    if ((s = check_cuda(cudaMemsetAsync(buf, 0, (size_t)off * sizeof(float), st), "scores pack")) != TT_OK) return s;
+    const int gx = (int)std::max<long long>(1, std::min<long long>((items + 255) / 256, std::max(1, 4 * 148 / n)));
+    k_scores_pack<<<dim3(gx, n), 256, 0, st>>>(B, rank, world, buf);
+    return check_launch("k_scores_pack");
 }
 
 tt_status tt_engine_sharded_scores_unpack(tt_engine* const* engines, int n, const float* buf, void* stream) {
     if (n <= 0) return TT_OK;
     if (!engines || !buf) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if (n > kMaxBatch) return set_error(TT_ERR_INVALID_ARGUMENT, "a sharded step takes at most %d engines.", kMaxBatch);
     for (int i = 0; i < n; ++i) {
         tt_status s = validate(engines[i]);
         if (s != TT_OK) return s;
     }
     DeviceGuard dg(engines[0]->cfg.device);
     cudaStream_t st = (cudaStream_t)stream;
-    size_t off = 0;
+    ScoreBatch B;
+    memset(&B, 0, sizeof(B));
+    B.n = n;
+    long long off = 0, longest = 1;
     for (int i = 0; i < n; ++i) {
-        tt_engine* e = engines[i];
-        const size_t msl = (size_t)e->cfg.max_seq_len;
-        tt_status s = check_cuda(cudaMemcpyAsync(e->g, buf + off, msl * sizeof(float), cudaMemcpyDeviceToDevice, st),
-                                 "scores unpack");
-        if (s != TT_OK) return s;
-        k_scores_refresh_hh<<<std::max(1, ceil_div(e->max_hh, 256)), 256, 0, st>>>(
-            reinterpret_cast<const MaintDesc*>(e->maint_dev));
-        if ((s = check_launch("k_scores_refresh_hh")) != TT_OK) return s;
-        off += msl;
+        B.d[i] = reinterpret_cast<const MaintDesc*>(engines[i]->maint_dev);
+        B.off[i] = off;
+        off += engines[i]->cfg.max_seq_len;
+        longest = std::max<long long>(longest, engines[i]->cfg.max_seq_len);
     }
-    return TT_OK;
+    const int gx = (int)std::max<long long>(1, std::min<long long>((longest + 255) / 256, std::max(1, 4 * 148 / n)));
+    k_scores_unpack<<<dim3(gx, n), 256, 0, st>>>(B, buf);
+    return check_launch("k_scores_unpack");
 }
 
 tt_status tt_engine_step_sharded_begin(tt_engine* const* engines, int n, const float* const* Q,
