@@ -92,29 +92,77 @@ __device__ __forceinline__ void copy_row(float* __restrict__ dst, const float* _
 }
 
 // k-th smallest (0-based) of x[0..n): 4 passes of an 8-bit radix histogram.
-// Returns the same value as std::nth_element (cache_engine.cpp:140-141).
+// Returns the same value as std::nth_element (cache_engine.cpp:140-141).  The
+// histograms are per warp (hist: [blockDim.x / 32][256] in shared memory), and
+// the lanes of a warp whose keys fall in one bin add once (match_any), so
+// equal scores -- most of them share their top bytes -- do not serialise on
+// one shared-memory word; warp 0 then sums the warps' histograms, 8 bins per
+// lane, and finds the bin holding k with one scan over the lanes.
+constexpr int kSelU = 16;  // candidates per thread per round of the radix select
 __device__ float block_select_kth(const float* __restrict__ x, int n, int k, unsigned int* hist) {
     __shared__ uint32_t s_prefix, s_k;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    unsigned int* hw = hist + warp * 256;
     uint32_t prefix = 0, mask = 0;
     if (threadIdx.x == 0) s_k = (uint32_t)k;
     for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+        for (int i = threadIdx.x; i < nw * 256; i += blockDim.x) hist[i] = 0;
         __syncthreads();
-        for (int i = threadIdx.x; i < n; i += blockDim.x) {
-            const uint32_t key = order_key(x[i]);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        // whole warps step together, kSelU loads in flight per thread (one CTA
+        // reads all the candidates four times: latency, not bandwidth, bounds it)
+        for (int base = warp * 32 * kSelU; base < n; base += blockDim.x * kSelU) {
+            float v[kSelU];
+#pragma unroll
+            for (int u = 0; u < kSelU; ++u) {
+                const int i = base + 32 * u + lane;
+                v[u] = i < n ? __ldcg(x + i) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < kSelU; ++u) {
+                uint32_t bin = 0xffffffffu;  // none
+                if (base + 32 * u + lane < n) {
+                    const uint32_t key = order_key(v[u]);
+                    if ((key & mask) == prefix) bin = (key >> shift) & 255u;
+                }
+                const unsigned grp = __match_any_sync(0xffffffffu, bin);
+                if (bin != 0xffffffffu && lane == __ffs(grp) - 1) atomicAdd(&hw[bin], (unsigned)__popc(grp));
+            }
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            uint32_t kk = s_k, cum = 0, d = 0;
-            for (d = 0; d < 256; ++d) {
-                if (kk < cum + hist[d]) break;
-                cum += hist[d];
+        if (warp == 0) {
+            uint32_t c[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                uint32_t t = 0;
+                for (int w = 0; w < nw; ++w) t += hist[w * 256 + lane * 8 + j];
+                c[j] = t;
+                tot += t;
             }
-            if (d > 255) d = 255;
-            s_k = kk - cum;
-            s_prefix = prefix | (d << shift);
+            uint32_t incl = tot;  // inclusive scan of the lanes' totals
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const uint32_t excl = incl - tot, kk = s_k;
+            const bool mine = kk >= excl && kk < incl;
+            const unsigned who = __ballot_sync(0xffffffffu, mine);
+            if (mine) {
+                uint32_t cum = excl;
+                int d = 0;
+                for (; d < 8; ++d) {
+                    if (kk < cum + c[d]) break;
+                    cum += c[d];
+                }
+                s_k = kk - cum;
+                s_prefix = prefix | ((uint32_t)(lane * 8 + d) << shift);
+            }
+            const uint32_t all = __shfl_sync(0xffffffffu, incl, 31);
+            if (who == 0 && lane == 0) {  // k at or past the count (not reached for k < n): the last bin
+                s_k = kk - all;
+                s_prefix = prefix | (255u << shift);
+            }
         }
         __syncthreads();
         prefix = s_prefix;
@@ -154,7 +202,7 @@ __device__ void flush_waiting_room(const MaintDesc& E, DevCounters& c) {
 __global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ MaintBatch B) {
     __shared__ MaintDesc E;
     __shared__ DevCounters c;
-    __shared__ unsigned int hist[256];
+    __shared__ unsigned int hist[(MT / 32) * 256];  // per-warp radix histograms
     __shared__ float s_red_v[MT / 32];
     __shared__ int s_red_i[MT / 32];
     __shared__ int s_action, s_mi;
