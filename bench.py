@@ -460,6 +460,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=2, choices=[1, 2, 5])
+    ap.add_argument("--exchange", default="nccl", choices=["nccl", "peer"],
+                    help="N>1: the per-step exchanges as NCCL all-gathers or over NVLink peer memory")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config3", action="store_true")
     ap.add_argument("--layers", type=int, default=None,
@@ -509,7 +511,7 @@ def ours_arm(args, cfg, rank, world, local, cores):
     history = []  # input set of every step the engines take (replayed by the parity check)
 
     if world > 1:
-        sharded = _C.ShardedEngineStep(engines, rank, world)
+        sharded = _C.ShardedEngineStep(engines, rank, world, exchange=args.exchange)
         step_fn = sharded
     else:
         step_fn = _C.engine_step_batched
@@ -677,6 +679,8 @@ def ours_arm(args, cfg, rank, world, local, cores):
 
     if world > 1:
         line["parity"] = sharded_parity(torch, dist, _C, cfg, engines, sharded, views, history, rank, world, msl)
+        line["exchange"] = sharded.exchange  # outside `config`, which both arms share
+        sharded.close()
         del sharded
     del engines
     torch.cuda.synchronize()

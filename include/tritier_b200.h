@@ -279,6 +279,36 @@ tt_status tt_engine_sharded_scores_pack(tt_engine* const* engines, int n, int ra
                                         void* stream);
 tt_status tt_engine_sharded_scores_unpack(tt_engine* const* engines, int n, const float* buf, void* stream);
 
+/* The same sharded step with the two per-step exchanges done by the library
+ * itself over NVLink peer memory (CUDA IPC) instead of by the caller's
+ * collectives: every rank owns an exchange region that all ranks write
+ * into, and the kernels wait for the other ranks' rows with bounded spins on
+ * step-numbered flags (a wait that runs out records TT_ERR_TIMEOUT in the
+ * engines' error word, reported by tt_engine_get_counters).  For the ranks of
+ * one node (2..8), one process per GPU:
+ *
+ *   tt_sharded_xch_create(world, rank, n, nq, hd, device, &x, handle)
+ *       handle: 64 bytes out (a CUDA IPC handle of this rank's region)
+ *   all-gather the handles in rank order (world * 64 bytes)
+ *   tt_sharded_xch_open(x, handles)
+ *   per step: [score synchronisation as above when needed, then route_valid = 0]
+ *       tt_engine_step_sharded_begin_xch(..., x, route_valid, stream)
+ *       tt_engine_step_sharded_merge_xch(..., x, attn_output, stream)
+ *   all ranks finished every step (e.g. a barrier), then tt_sharded_xch_destroy(x)
+ *
+ * route_valid = 0 on the first step and after a score synchronisation (the
+ * same rule as route_all = NULL above); every rank makes the same calls. */
+typedef struct tt_xch tt_xch;
+tt_status tt_sharded_xch_create(int world, int rank, int max_engines, int num_q_heads, int head_dim, int device,
+                                tt_xch** out, void* ipc_handle);
+tt_status tt_sharded_xch_open(tt_xch* x, const void* ipc_handles);
+tt_status tt_sharded_xch_destroy(tt_xch* x);
+tt_status tt_engine_step_sharded_begin_xch(tt_engine* const* engines, int n, const float* const* Q,
+                                           const float* const* K_new, const float* const* V_new, tt_xch* x,
+                                           int route_valid, void* stream);
+tt_status tt_engine_step_sharded_merge_xch(tt_engine* const* engines, int n, tt_xch* x,
+                                           float* const* attn_output, void* stream);
+
 /* Replaces TriTierCacheEngine::prefill (cache_engine.cpp:271-395; binding
  * bindings.cpp:418-436): K_all/V_all [q_len, num_kv_heads, head_dim].
  * q_len < 0 -> TT_ERR_INVALID_ARGUMENT. */

@@ -614,6 +614,40 @@ class ShardedStep:
                                                      self._ptrs(outs, "attn_output"), route_send.data_ptr(),
                                                      _stream()), "merge")
 
+    # -- peer-memory exchange (tt_sharded_xch_*): the library exchanges the rows
+    def xch_create(self) -> bytes:
+        """Allocates this rank's exchange region; returns its 64-byte IPC handle."""
+        x = C.c_void_p()
+        h = (C.c_char * 64)()
+        dev = self.engines[0]._dev
+        with torch.cuda.device(dev):
+            check(lib().tt_sharded_xch_create(self.world, self.rank, self.n, self.nq, self.hd, dev, C.byref(x), h),
+                  "xch_create")
+        self._x = x
+        return bytes(h)
+
+    def xch_open(self, handles: bytes) -> None:
+        """Opens the other ranks' regions (handles: world x 64 bytes, rank order)."""
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_sharded_xch_open(self._x, handles), "xch_open")
+
+    def xch_destroy(self) -> None:
+        x = getattr(self, "_x", None)
+        if x:
+            lib().tt_sharded_xch_destroy(x)
+            self._x = None
+
+    def begin_xch(self, Qs, Ks, Vs, route_valid: bool) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_step_sharded_begin_xch(self._hs, self.n, self._ptrs(Qs, "Q"),
+                                                         self._ptrs(Ks, "K_new"), self._ptrs(Vs, "V_new"), self._x,
+                                                         1 if route_valid else 0, _stream()), "begin_xch")
+
+    def merge_xch(self, outs) -> None:
+        with torch.cuda.device(self.engines[0]._dev):
+            check(lib().tt_engine_step_sharded_merge_xch(self._hs, self.n, self._x, self._ptrs(outs, "attn_output"),
+                                                         _stream()), "merge_xch")
+
 
 class ShardedEngineStep:
     """engine_step_batched over the ranks of a torch.distributed process group
@@ -629,8 +663,13 @@ class ShardedEngineStep:
     phases (device time per phase, phase_times())."""
 
     PHASES = ("sync", "begin", "allgather_rows", "merge", "allgather_route")
+    PHASES_PEER = ("sync", "begin", "merge")
 
-    def __init__(self, engines, rank=None, world=None, group=None):
+    def __init__(self, engines, rank=None, world=None, group=None, exchange="nccl"):
+        """exchange: "nccl" (two all-gathers of the process group per step) or
+        "peer" (the library writes the rows into every rank's memory over
+        NVLink and waits on flags; ranks of one node, 2..8; call close() on
+        every rank when done)."""
         import torch.distributed as dist
         self.group = group
         self.world = dist.get_world_size(group) if world is None else int(world)
@@ -638,6 +677,19 @@ class ShardedEngineStep:
         self.engines = list(engines)
         self.step = ShardedStep(self.engines, self.rank, self.world)
         self.dev = self.engines[0].device
+        if exchange not in ("nccl", "peer"):
+            raise ValueError("exchange must be 'nccl' or 'peer'.")
+        self.exchange = exchange if self.world > 1 else "nccl"
+        if self.exchange == "peer":
+            self.PHASES = self.PHASES_PEER
+            h = torch.tensor(list(self.step.xch_create()), dtype=torch.uint8, device=self.dev)
+            allh = torch.empty(self.world * 64, dtype=torch.uint8, device=self.dev)
+            dist.all_gather_into_tensor(allh, h, group=self.group)
+            self.step.xch_open(bytes(allh.cpu().numpy().tobytes()))
+            # a rank that leaves without close() (an exception) still waits for
+            # the others at exit before its region goes away
+            import atexit
+            atexit.register(self.close)
         st = self.step
         self.xs = torch.empty(st.xch_floats, device=self.dev)
         self.xa = torch.empty(self.world * st.xch_floats, device=self.dev)
@@ -664,6 +716,17 @@ class ShardedEngineStep:
         self._pending = []
         return {p: round(v / max(steps, 1), 5) for p, v in self._acc.items()}
 
+    def close(self) -> None:
+        """Peer exchange: wait for every rank to finish its steps, then free the
+        exchange regions (no rank may free its region while another can still
+        write into it)."""
+        import torch.distributed as dist
+        if self.exchange == "peer" and getattr(self.step, "_x", None):
+            torch.cuda.synchronize(self.dev)
+            if dist.is_initialized():
+                dist.barrier(group=self.group)
+            self.step.xch_destroy()
+
     def __call__(self, engines, Qs, Ks, Vs, outs) -> None:
         import torch.distributed as dist
         if len(engines) != self.step.n or any(a is not b for a, b in zip(engines, self.engines)):
@@ -673,6 +736,27 @@ class ShardedEngineStep:
         if self._timing:
             ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)]
             ev[0].record()
+        if self.exchange == "peer":
+            route_valid = self.route_valid
+            if st.sync_needed():
+                if self.scores is None:
+                    self.scores = torch.empty(st.scores_floats(), device=self.dev)
+                st.scores_pack(self.scores)
+                dist.all_reduce(self.scores, group=self.group)
+                st.scores_unpack(self.scores)
+                route_valid = False
+                self.syncs += 1
+            if ev:
+                ev[1].record()
+            st.begin_xch(Qs, Ks, Vs, route_valid)
+            if ev:
+                ev[2].record()
+            st.merge_xch(outs)
+            self.route_valid = True
+            if ev:
+                ev[3].record()
+                self._pending.append(ev)
+            return
         route = self.ra if self.route_valid else None
         if self.world > 1 and st.sync_needed():
             if self.scores is None:

@@ -63,7 +63,9 @@ EXPORTS = [
     "tt_engine_device_bytes", "tt_engine_set_counters", "tt_profile_enable", "tt_profile_collect",
     "tt_device_error", "tt_fused_attention_decode_noalloc", "tt_engine_step_sharded_begin",
     "tt_engine_step_sharded_merge", "tt_engine_sharded_sync_needed", "tt_engine_sharded_scores_floats",
-    "tt_engine_sharded_scores_pack", "tt_engine_sharded_scores_unpack",
+    "tt_engine_sharded_scores_pack", "tt_engine_sharded_scores_unpack", "tt_sharded_xch_create",
+    "tt_sharded_xch_open", "tt_sharded_xch_destroy", "tt_engine_step_sharded_begin_xch",
+    "tt_engine_step_sharded_merge_xch",
     "tt_engine_ingest", "tt_engine_full_count", "tt_engine_reconstruct", "tt_engine_accumulate_scores",
 ]
 
@@ -107,6 +109,11 @@ def _declare(L):
     L.tt_engine_sharded_scores_floats.argtypes = [pv, i, C.POINTER(C.c_longlong)]
     L.tt_engine_sharded_scores_pack.argtypes = [pv, i, i, i, vp, vp]
     L.tt_engine_sharded_scores_unpack.argtypes = [pv, i, vp, vp]
+    L.tt_sharded_xch_create.argtypes = [i, i, i, i, i, i, C.POINTER(vp), vp]
+    L.tt_sharded_xch_open.argtypes = [vp, vp]
+    L.tt_sharded_xch_destroy.argtypes = [vp]
+    L.tt_engine_step_sharded_begin_xch.argtypes = [pv, i, pv, pv, pv, vp, i, vp]
+    L.tt_engine_step_sharded_merge_xch.argtypes = [pv, i, vp, pv, vp]
     L.tt_engine_ingest.argtypes = [vp, vp, vp, vp]
     L.tt_engine_full_count.argtypes = [vp, C.POINTER(i)]
     L.tt_engine_reconstruct.argtypes = [vp, vp, vp, vp, i, C.POINTER(i), vp]

@@ -275,6 +275,27 @@ __global__ void __launch_bounds__(NT) k_shard_local_merge(const __grid_constant_
     }
 }
 
+// Peer exchange after k_shard_local_merge: this rank's rows of job
+// blockIdx.x, already in its own region's slot, copied into every other
+// rank's region, then the job's flag set on every rank.  grid (njobs).
+__global__ void __launch_bounds__(NT) k_publish_rows(const __grid_constant__ AttnLaunch L) {
+    const int job = blockIdx.x;
+    const int nq = L.inline_job.nq, HD = L.inline_job.hd;
+    const size_t n = (size_t)nq * (HD + 2), off = ((size_t)L.px.rank * L.px.jobs + job) * n;
+    const float* src = L.px.rows[L.px.rank] + off;
+    for (int p = 0; p < L.px.world; ++p) {
+        if (p == L.px.rank) continue;
+        float* dst = L.px.rows[p] + off;
+        for (size_t i = threadIdx.x; i < n; i += NT) dst[i] = src[i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        for (int p = 0; p < L.px.world; ++p)
+            st_release_sys(L.px.flags[p] + (size_t)L.px.rank * L.px.jobs + job, (unsigned long long)L.px.step);
+    }
+}
+
 // Phase 2: every rank's rows -> output (ranks merged in order 0..world-1, so
 // all ranks produce the same bits), the decayed score feedback
 // g[id] = decay g[id] + w of the tokens this rank owns (cache_engine.cpp:
@@ -291,12 +312,23 @@ __global__ void __launch_bounds__(NT, 3) k_shard_merge(const __grid_constant__ A
     if (threadIdx.x == 0) Js = L.jobs[job] ? *L.jobs[job] : L.inline_job;
     __syncthreads();
     const JobDesc& J = Js;
-    if (threadIdx.x == 0) Ts = resolve_counts(J);  // overlaps the row reads below
+    const bool peer = L.px.world > 1;
+    if (threadIdx.x == 0) {
+        Ts = resolve_counts(J);
+        // peer exchange: every rank's rows of this job have landed in this
+        // rank's region (bounded wait; on expiry the error is recorded and
+        // the step's results are not valid)
+        if (peer && !wait_peer_flags(L.px.flags[L.px.rank] + job, L.px.jobs, L.px.world, L.px.step)) {
+            atomicCAS(&g_device_error, 0, (int)TT_ERR_TIMEOUT);
+            if (J.ctr) atomicCAS(const_cast<int*>(&J.ctr->error), 0, (int)TT_ERR_TIMEOUT);
+        }
+    }
+    __syncthreads();
     const int nq = J.nq, HD = J.hd, P = L.world;
     float* Ms = sm;
     float* IL = sm + nq;
-    const size_t row = (size_t)HD + 2, rstride = (size_t)L.njobs * nq * row;
-    const float* base = xch_all + (size_t)job * nq * row;
+    const size_t row = (size_t)HD + 2, rstride = (size_t)(peer ? L.px.jobs : L.njobs) * nq * row;
+    const float* base = (peer ? L.px.rows[L.px.rank] : xch_all) + (size_t)job * nq * row;
     // (M, 1/L) of every head: 8 adjacent threads per head, each holding the
     // (m, l) pairs of ranks sub, sub + 8, ... (one load round for P <= 8)
     for (int h0 = 0; h0 < nq; h0 += NT / 8) {
@@ -423,7 +455,16 @@ __global__ void __launch_bounds__(NT, 3) k_shard_merge(const __grid_constant__ A
                 const long long id = (long long)tc.total - tc.ring_size;
                 if (id >= 0 && id < J.msl) rr.ev_score = __ldcg(J.g + id);
             }
-            route[job] = rr;
+            if (peer) {  // into every rank's region at this rank's slot, then the flags
+                for (int p = 0; p < L.px.world; ++p)
+                    reinterpret_cast<RouteRow*>(L.px.route[p])[(size_t)L.px.rank * L.px.jobs + job] = rr;
+                __threadfence_system();
+                for (int p = 0; p < L.px.world; ++p)
+                    st_release_sys(L.px.flags[p] + (size_t)(L.px.world + L.px.rank) * L.px.jobs + job,
+                                   (unsigned long long)L.px.step);
+            } else {
+                route[job] = rr;
+            }
             *job_counter(J) = 0;
         }
     }
@@ -619,9 +660,18 @@ tt_status launch_sharded_partial(const AttnLaunch& L, float* xch, cudaStream_t s
     if (s != TT_OK) return s;
     dim3 grid(L.inline_job.nq, L.njobs);
     const int ps = prof_begin(2, st);  // the sharded epilogue kernels count as finalize
-    k_shard_local_merge<<<grid, NT, (size_t)(L.nd + L.np + 1) * sizeof(float), st>>>(L, xch);
+    // peer exchange: the rows go to this rank's slot of its own region first
+    float* dst = L.px.world > 1
+                     ? L.px.rows[L.px.rank] + (size_t)L.px.rank * L.px.jobs * L.inline_job.nq * (L.inline_job.hd + 2)
+                     : xch;
+    k_shard_local_merge<<<grid, NT, (size_t)(L.nd + L.np + 1) * sizeof(float), st>>>(L, dst);
+    tt_status s2 = check_launch("k_shard_local_merge");
+    if (s2 == TT_OK && L.px.world > 1) {
+        k_publish_rows<<<L.njobs, NT, 0, st>>>(L);
+        s2 = check_launch("k_publish_rows");
+    }
     prof_end(ps, st);
-    return check_launch("k_shard_local_merge");
+    return s2;
 }
 
 tt_status launch_sharded_merge(const AttnLaunch& L, const float* xch_all, RouteRow* route, int pos_cap,

@@ -78,6 +78,22 @@ __device__ __forceinline__ TierCounts resolve_counts(const JobDesc& j) {
 // Host-side launch description.
 constexpr int kMaxBatch = 64;
 
+// Peer-memory exchange of a sequence-sharded step (one node, CUDA IPC over
+// NVLink; world > 1 enables it).  Every rank owns a region that all ranks
+// write into: rows [world][jobs][nq][hd + 2] floats, routing rows
+// [world][jobs] and flags [2][world][jobs] (u64): flag[0][p][j] is the last
+// step whose exchange rows rank p has published for job j, flag[1][p][j] the
+// same for its routing row.  rows[p] / route[p] / flags[p] are rank p's region
+// as this rank addresses it (its own for p == rank).
+constexpr int kMaxWorld = 8;
+struct PeerXch {
+    int world, rank, jobs;  // jobs: the regions' job capacity (stride of the rank slots)
+    long long step;         // the step being run (flags start at 0, steps at 1)
+    float* rows[kMaxWorld];
+    void* route[kMaxWorld];
+    unsigned long long* flags[kMaxWorld];
+};
+
 struct AttnLaunch {
     int njobs;
     int nhg;      // kv-head groups per job (grid.y = njobs * nhg)
@@ -95,6 +111,7 @@ struct AttnLaunch {
     // zero); the launch functions pick the mode per launch.
     int merge_mode;
     float* xch;      // merge_mode 2: [njobs][nq][hd + 2] (m, l, acc) rows
+    PeerXch px;      // merge_mode 2 with px.world > 1: the rows go to every rank's region
     const JobDesc* jobs[kMaxBatch];  // device descriptor per job (engines) or nullptr
     JobDesc inline_job;              // stand-alone job (jobs[0] == nullptr, njobs == 1)
     const float* Q[kMaxBatch];
@@ -188,6 +205,30 @@ struct RouteRow {
     int hh_slot;
     int pad;
 };
+
+// Flags across GPUs (system scope): a release store after the data it
+// publishes, an acquire load before reading the data it guards.
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Waits until f[q * stride] >= target for q < count; bounded (2^22 polls
+// with a 256 ns sleep: a few seconds at most).  False if a wait ran out.
+constexpr int kPeerSpin = 1 << 22;
+__device__ __forceinline__ bool wait_peer_flags(const unsigned long long* f, int stride, int count, long long target) {
+    for (int q = 0; q < count; ++q) {
+        int it = 0;
+        while ((long long)ld_acquire_sys(f + (size_t)q * stride) < target) {
+            if (++it >= kPeerSpin) return false;
+            __nanosleep(256);
+        }
+    }
+    return true;
+}
 
 // Scratch a job needs for a given plan: chunk slots and score stride.
 int attn_max_chunks(int dense_cap, int pbs_tok_cap);

@@ -53,6 +53,18 @@ struct tt_engine {
     cudaStream_t last_stream = nullptr;
 };
 
+// Peer-memory exchange of sequence-sharded steps: this rank's region (rows,
+// routing rows, flags; see PeerXch) and the other ranks' regions opened
+// through CUDA IPC.
+struct tt_xch {
+    int world = 0, rank = 0, jobs = 0, nq = 0, hd = 0, device = 0;
+    size_t rows_bytes = 0, route_bytes = 0, flags_bytes = 0;
+    char* base = nullptr;                       // own region
+    char* peer[tt::kMaxWorld] = {nullptr};      // opened regions of the other ranks
+    long long step = 0;
+    bool opened = false;
+};
+
 namespace tt {
 
 // Per-engine constants and pointers read by the maintenance kernel.
@@ -74,6 +86,9 @@ struct MaintBatch {
     // current for every token).
     const RouteRow* route;
     int world;
+    int route_stride;                      // rows between ranks' slots of `route`
+    const unsigned long long* route_flags; // peer exchange: wait for flags[q * route_stride + job] >= route_step
+    long long route_step;
     const MaintDesc* d[kMaxBatch];
     const float* K[kMaxBatch];
     const float* V[kMaxBatch];
@@ -209,6 +224,11 @@ __global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ 
     __shared__ float s_score;
     if (threadIdx.x == 0) {
         E = *B.d[blockIdx.x];
+        // peer exchange: every rank's routing row of the last step has landed
+        if (B.route && B.route_flags &&
+            !wait_peer_flags(B.route_flags + blockIdx.x, B.route_stride, B.world, B.route_step)) {
+            atomicCAS(&E.ctr->error, 0, (int)TT_ERR_TIMEOUT);  // the engine's sticky error
+        }
         c = *E.ctr;
     }
     __syncthreads();
@@ -254,7 +274,7 @@ __global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ 
             if (B.route) {
                 // the ring slot's owner published the score; every rank stores
                 // it, so the token's score is current wherever it moves next
-                s_score = B.route[(size_t)(slot % B.world) * B.n + blockIdx.x].ev_score;
+                s_score = B.route[(size_t)(slot % B.world) * B.route_stride + blockIdx.x].ev_score;
                 if (id >= 0 && id < E.msl) E.g[id] = s_score;
             } else {
                 s_score = (id >= 0 && id < E.msl) ? E.g[id] : 0.f;
@@ -274,7 +294,7 @@ __global__ void __launch_bounds__(MT) k_engine_maintain(const __grid_constant__ 
                     float v0 = INFINITY;
                     int i0 = -1;
                     for (int p = 0; p < B.world; ++p) {
-                        const RouteRow rr = B.route[(size_t)p * B.n + blockIdx.x];
+                        const RouteRow rr = B.route[(size_t)p * B.route_stride + blockIdx.x];
                         if (rr.hh_slot >= 0 && (i0 < 0 || rr.hh_min < v0 || (rr.hh_min == v0 && rr.hh_slot < i0))) {
                             v0 = rr.hh_min;
                             i0 = rr.hh_slot;
@@ -905,12 +925,17 @@ long long step_block_bound(const tt_engine* e) {
 // Maintenance of engines[0..m) in one launch; returns the dense and packed
 // token capacities the attention launch must cover.
 tt_status maintain_batch(tt_engine* const* engines, int m, const float* const* K_new, const float* const* V_new,
-                         cudaStream_t st, int& dcap, int& pcap, const RouteRow* route = nullptr, int world = 1) {
+                         cudaStream_t st, int& dcap, int& pcap, const RouteRow* route = nullptr, int world = 1,
+                         int route_stride = 0, const unsigned long long* route_flags = nullptr,
+                         long long route_step = 0) {
     MaintBatch mb;
     memset(&mb, 0, sizeof(mb));
     mb.n = m;
     mb.route = route;
     mb.world = world;
+    mb.route_stride = route_stride > 0 ? route_stride : m;
+    mb.route_flags = route_flags;
+    mb.route_step = route_step;
     dcap = 0;
     pcap = 0;
     for (int i = 0; i < m; ++i) {
@@ -1180,6 +1205,175 @@ tt_status tt_engine_step_sharded_merge(tt_engine* const* engines, int n, int ran
     return launch_sharded_merge(L, xch_all, static_cast<RouteRow*>(route_send), pos_cap, (cudaStream_t)stream);
 }
 
+tt_status tt_sharded_xch_create(int world, int rank, int max_engines, int num_q_heads, int head_dim, int device,
+                                tt_xch** out, void* ipc_handle) {
+    if (!out || !ipc_handle) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if (world < 2 || world > kMaxWorld || rank < 0 || rank >= world)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "peer exchange needs 2..%d ranks (rank %d of %d).", kMaxWorld, rank,
+                         world);
+    if (max_engines <= 0 || max_engines > kMaxBatch || num_q_heads <= 0 || head_dim <= 0)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "invalid exchange size.");
+    DeviceGuard dg(device);
+    tt_xch* x = new (std::nothrow) tt_xch();
+    if (!x) return set_error(TT_ERR_OUT_OF_MEMORY, "out of host memory.");
+    x->world = world; x->rank = rank; x->jobs = max_engines; x->nq = num_q_heads; x->hd = head_dim; x->device = device;
+    auto a256 = [](size_t b) { return (b + 255) / 256 * 256; };
+    x->rows_bytes = a256((size_t)world * max_engines * num_q_heads * (head_dim + 2) * sizeof(float));
+    x->route_bytes = a256((size_t)world * max_engines * sizeof(RouteRow));
+    x->flags_bytes = a256((size_t)2 * world * max_engines * sizeof(unsigned long long));
+    const size_t total = x->rows_bytes + x->route_bytes + x->flags_bytes;
+    tt_status s = check_cuda(cudaMalloc(&x->base, total), "cudaMalloc(exchange region)");
+    if (s == TT_OK) s = check_cuda(cudaMemset(x->base, 0, total), "exchange region clear");
+    if (s == TT_OK) s = check_cuda(cudaDeviceSynchronize(), "exchange region clear");
+    cudaIpcMemHandle_t h;
+    if (s == TT_OK) s = check_cuda(cudaIpcGetMemHandle(&h, x->base), "cudaIpcGetMemHandle");
+    if (s != TT_OK) {
+        if (x->base) cudaFree(x->base);
+        delete x;
+        return s;
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *out = x;
+    return TT_OK;
+}
+
+tt_status tt_sharded_xch_open(tt_xch* x, const void* ipc_handles) {
+    if (!x || !ipc_handles) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    if (x->opened) return set_error(TT_ERR_INVALID_ARGUMENT, "exchange already opened.");
+    DeviceGuard dg(x->device);
+    const char* hs = static_cast<const char*>(ipc_handles);
+    for (int p = 0; p < x->world; ++p) {
+        if (p == x->rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hs + (size_t)p * sizeof(h), sizeof(h));
+        void* ptr = nullptr;
+        tt_status s = check_cuda(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        if (s != TT_OK) {
+            for (int q = 0; q < p; ++q)
+                if (x->peer[q]) cudaIpcCloseMemHandle(x->peer[q]);
+            return s;
+        }
+        x->peer[p] = static_cast<char*>(ptr);
+    }
+    x->opened = true;
+    return TT_OK;
+}
+
+tt_status tt_sharded_xch_destroy(tt_xch* x) {
+    if (!x) return TT_OK;
+    DeviceGuard dg(x->device);
+    cudaDeviceSynchronize();
+    for (int p = 0; p < x->world; ++p)
+        if (x->peer[p]) cudaIpcCloseMemHandle(x->peer[p]);
+    if (x->base) cudaFree(x->base);
+    delete x;
+    return TT_OK;
+}
+
+namespace {
+// The exchange description the kernels get for step x->step.
+PeerXch peer_xch(const tt_xch* x) {
+    PeerXch px;
+    memset(&px, 0, sizeof(px));
+    px.world = x->world; px.rank = x->rank; px.jobs = x->jobs; px.step = x->step;
+    for (int p = 0; p < x->world; ++p) {
+        char* b = p == x->rank ? x->base : x->peer[p];
+        px.rows[p] = reinterpret_cast<float*>(b);
+        px.route[p] = b + x->rows_bytes;
+        px.flags[p] = reinterpret_cast<unsigned long long*>(b + x->rows_bytes + x->route_bytes);
+    }
+    return px;
+}
+
+tt_status validate_xch(const tt_xch* x, tt_engine* const* engines, int n) {
+    if (!x || !x->opened) return set_error(TT_ERR_INVALID_ARGUMENT, "exchange not created and opened.");
+    if (n > x->jobs) return set_error(TT_ERR_INVALID_ARGUMENT, "%d engines but the exchange holds %d.", n, x->jobs);
+    const tt_engine_config& c = engines[0]->cfg;
+    if (c.num_q_heads != x->nq || c.head_dim != x->hd || c.device != x->device)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "exchange built for other heads, head_dim or device.");
+    return TT_OK;
+}
+}  // namespace
+
+tt_status tt_engine_step_sharded_begin_xch(tt_engine* const* engines, int n, const float* const* Q,
+                                           const float* const* K_new, const float* const* V_new, tt_xch* x,
+                                           int route_valid, void* stream) {
+    if (n <= 0) return TT_OK;
+    if (!x) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_status s = validate_shard_args(engines, n, x->rank, x->world);
+    if (s != TT_OK) return s;
+    if ((s = validate_xch(x, engines, n)) != TT_OK) return s;
+    s = validate_step(engines, n, Q, K_new, V_new);
+    if (s != TT_OK) return s;
+    if (route_valid)
+        for (int i = 0; i < n; ++i)
+            if (step_recomputes_threshold(engines[i]))
+                return set_error(TT_ERR_INVALID_ARGUMENT,
+                                 "this step recomputes the heavy-hitter threshold: synchronise the scores "
+                                 "(tt_engine_sharded_scores_pack / _unpack) and pass route_valid = 0.");
+    if (route_valid && x->step == 0)
+        return set_error(TT_ERR_INVALID_ARGUMENT, "no routing rows yet: the first step takes route_valid = 0.");
+    DeviceGuard dg(engines[0]->cfg.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    x->step += 1;
+    const PeerXch px = peer_xch(x);
+    int dcap = 0, pcap = 0;
+    const RouteRow* route = route_valid ? static_cast<const RouteRow*>(px.route[x->rank]) : nullptr;
+    s = maintain_batch(engines, n, K_new, V_new, st, dcap, pcap, route, x->world, x->jobs,
+                       px.flags[x->rank] + (size_t)x->world * x->jobs, x->step - 1);
+    if (s != TT_OK) return s;
+    AttnLaunch L;
+    memset(&L, 0, sizeof(L));
+    L.njobs = n;
+    const tt_engine_config& c0 = engines[0]->cfg;
+    int dcap_r = 0, pcap_r = 0;
+    for (int i = 0; i < n; ++i) {
+        int d = 0, p = 0;
+        shard_caps(engines[i], step_block_bound(engines[i]), x->world, d, p);
+        dcap_r = std::max(dcap_r, d);
+        pcap_r = std::max(pcap_r, p);
+    }
+    s = plan_attention(L, c0.num_q_heads, c0.num_kv_heads, c0.head_dim, dcap_r, pcap_r);
+    if (s != TT_OK) return s;
+    L.PC = ceil_div(L.PC, kShardGran) * kShardGran;
+    L.np = ceil_div(pcap_r, L.PC);
+    fill_launch(L, engines, n, Q, nullptr);
+    L.rank = x->rank;
+    L.world = x->world;
+    L.merge_mode = 1;
+    L.px = px;
+    s = launch_sharded_partial(L, nullptr, st);
+    if (s != TT_OK) return s;
+    advance_mirrors(engines, n, st);
+    return TT_OK;
+}
+
+tt_status tt_engine_step_sharded_merge_xch(tt_engine* const* engines, int n, tt_xch* x, float* const* attn_output,
+                                           void* stream) {
+    if (n <= 0) return TT_OK;
+    if (!x || !attn_output) return set_error(TT_ERR_INVALID_ARGUMENT, "NULL argument.");
+    tt_status s = validate_shard_args(engines, n, x->rank, x->world);
+    if (s != TT_OK) return s;
+    if ((s = validate_xch(x, engines, n)) != TT_OK) return s;
+    if (x->step == 0) return set_error(TT_ERR_INVALID_ARGUMENT, "merge before the first begin.");
+    for (int i = 0; i < n; ++i)
+        if (!attn_output[i]) return set_error(TT_ERR_INVALID_ARGUMENT, "attn_output must not be NULL.");
+    DeviceGuard dg(engines[0]->cfg.device);
+    AttnLaunch L;
+    memset(&L, 0, sizeof(L));
+    fill_launch(L, engines, n, nullptr, attn_output);
+    L.rank = x->rank;
+    L.world = x->world;
+    L.px = peer_xch(x);
+    int pos_cap = 0;
+    for (int i = 0; i < n; ++i) {  // the mirrors already count the step begun
+        int d = 0, p = 0;
+        shard_caps(engines[i], engines[i]->h_wr_pbs_ub / engines[i]->chunk, x->world, d, p);
+        pos_cap = std::max(pos_cap, d + p);
+    }
+    return launch_sharded_merge(L, nullptr, nullptr, pos_cap, (cudaStream_t)stream);
+}
+
 tt_status tt_engine_step(tt_engine* e, const float* Q, const float* K_new, const float* V_new, float* attn_output,
                          void* stream) {
     return tt_engine_step_batched(&e, 1, &Q, &K_new, &V_new, &attn_output, stream);
@@ -1341,7 +1535,9 @@ tt_status tt_engine_get_counters(tt_engine* e, tt_engine_counters* out) {
     if ((s = check_cuda(cudaStreamSynchronize(e->last_stream), "engine sync")) != TT_OK) return s;
     DevCounters c;
     if ((s = check_cuda(cudaMemcpy(&c, e->ctr, sizeof(c), cudaMemcpyDeviceToHost), "counter read")) != TT_OK) return s;
-    if (c.error) return set_error((tt_status)c.error, "device-side engine error %d (packed capacity)", c.error);
+    if (c.error)
+        return set_error((tt_status)c.error, "device-side engine error %d (%s)", c.error,
+                         c.error == TT_ERR_TIMEOUT ? "a bounded wait ran out" : "packed capacity");
     out->s_count = c.s_count;
     out->rw_count = c.rw_count;
     out->rw_head_index = c.rw_head;

@@ -873,18 +873,25 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
             }
         }
         if (L.merge_mode == 2) {
-            float* xr = L.xch + ((size_t)job * nq + h) * (HD + 2);
+            // the job's row: into the exchange buffer, or into every rank's
+            // region (peer memory over NVLink) at this rank's slot
+            const int nw = L.px.world > 1 ? L.px.world : 1;
+            for (int p = 0; p < nw; ++p) {
+                float* xr = L.px.world > 1
+                                ? L.px.rows[p] + (((size_t)L.px.rank * L.px.jobs + job) * nq + h) * (HD + 2)
+                                : L.xch + ((size_t)job * nq + h) * (HD + 2);
 #pragma unroll
-            for (int v = 0; v < V4; ++v) {
-                const int c = 4 * (tq + TPH * v);
-                xr[2 + c] = o[v].x;
-                xr[3 + c] = o[v].y;
-                xr[4 + c] = o[v].z;
-                xr[5 + c] = o[v].w;
-            }
-            if (tq == 0) {
-                xr[0] = M;
-                xr[1] = S;
+                for (int v = 0; v < V4; ++v) {
+                    const int c = 4 * (tq + TPH * v);
+                    xr[2 + c] = o[v].x;
+                    xr[3 + c] = o[v].y;
+                    xr[4 + c] = o[v].z;
+                    xr[5 + c] = o[v].w;
+                }
+                if (tq == 0) {
+                    xr[0] = M;
+                    xr[1] = S;
+                }
             }
             if (threadIdx.x == 0 && h == 0) *route_min_word(J) = 0ull;
         } else {
@@ -910,6 +917,14 @@ __device__ __forceinline__ void chunk_merge_tail(const AttnLaunch& L, const JobD
                 ml[2 * h] = M;
                 ml[2 * h + 1] = inv;
             }
+        }
+    }
+    if (L.merge_mode == 2 && L.px.world > 1) {
+        __syncthreads();  // every thread's row stores are issued before the flags
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            for (int p = 0; p < L.px.world; ++p)
+                st_release_sys(L.px.flags[p] + (size_t)L.px.rank * L.px.jobs + job, (unsigned long long)L.px.step);
         }
     }
     if (threadIdx.x == 0) *job_counter(J) = 0;
