@@ -303,6 +303,26 @@ class _FakeStep:
         rs.fill_(10 * self.step_no + self.rank)
         self.step_no += 1
 
+    # peer exchange
+    def xch_create(self):
+        self.calls.append("xch_create")
+        self._x = True
+        return bytes([self.rank]) * 64
+
+    def xch_open(self, handles):
+        self.calls.append(("xch_open", handles))
+
+    def xch_destroy(self):
+        self.calls.append("xch_destroy")
+        self._x = None
+
+    def begin_xch(self, Qs, Ks, Vs, route_valid):
+        self.calls.append(("begin_xch", route_valid))
+
+    def merge_xch(self, outs):
+        self.calls.append("merge_xch")
+        self.step_no += 1
+
 
 class _FakeEngine:
     def __init__(self):
@@ -310,7 +330,7 @@ class _FakeEngine:
         self.device = torch.device("cpu")
 
 
-def _driver_rank(rank, world, port, q):
+def _driver_rank(rank, world, port, q, exchange="nccl"):
     try:
         import torch.distributed as dist
         from datetime import timedelta
@@ -319,9 +339,10 @@ def _driver_rank(rank, world, port, q):
                                 timeout=timedelta(seconds=60))
         _C.ShardedStep = _FakeStep
         engines = [_FakeEngine(), _FakeEngine()]
-        drv = _C.ShardedEngineStep(engines)
+        drv = _C.ShardedEngineStep(engines, exchange=exchange)
         for _ in range(5):
             drv(engines, [None] * 2, [None] * 2, [None] * 2, [None] * 2)
+        drv.close()
         calls = drv.step.calls
         dist.destroy_process_group()
         q.put((rank, (calls, drv.syncs), None))
@@ -351,3 +372,29 @@ def test_sharded_driver_collective_sequence():
             op, xa = next(it)
             assert op == "merge"
             assert xa == [100.0 * step + p for p in range(world) for _ in range(12)]
+
+
+def _driver_rank_peer(rank, world, port, q):
+    _driver_rank(rank, world, port, q, exchange="peer")
+
+
+def test_sharded_driver_peer_exchange_sequence():
+    world = 2
+    res = _run_ranks(_driver_rank_peer, world, ())
+    for r in range(world):
+        calls, syncs = res[r]
+        assert syncs == 2
+        it = iter(calls)
+        assert next(it) == "xch_create"
+        op, handles = next(it)  # every rank's handle, in rank order
+        assert op == "xch_open" and handles == b"".join(bytes([p]) * 64 for p in range(world))
+        for step in range(5):
+            if step % 3 == 0:
+                assert next(it) == "pack"
+                op, buf = next(it)
+                assert op == "unpack" and buf == [float(i * 3) for i in range(5)]
+            # routing rows from the last step, except on the first step and after a synchronisation
+            assert next(it) == ("begin_xch", step % 3 != 0)
+            assert next(it) == "merge_xch"
+        assert next(it) == "xch_destroy"
+        assert next(it, None) is None

@@ -722,7 +722,8 @@ class ShardedEngineStep:
         write into it)."""
         import torch.distributed as dist
         if self.exchange == "peer" and getattr(self.step, "_x", None):
-            torch.cuda.synchronize(self.dev)
+            if self.dev.type == "cuda":
+                torch.cuda.synchronize(self.dev)
             if dist.is_initialized():
                 dist.barrier(group=self.group)
             self.step.xch_destroy()
