@@ -719,11 +719,11 @@ tt_status launch_attention(const AttnLaunch& L, cudaStream_t st) {
         tt_status s = check_launch("k_attn_merge_heads");
         if (s != TT_OK) return s;
     }
-    // positions: at most nd * DC dense + np * PC packed; about eight CTAs per
-    // SM over the launch (several waves of short CTAs: each thread's chain of
-    // dependent loads is short), each striding over its job's positions
+    // positions: at most nd * DC dense + np * PC packed; one wave over the
+    // launch (4 CTAs per SM), each CTA striding over its job's positions four
+    // per thread (measured on config 2: 38.4 -> 36.3 us against two waves)
     const long long tcap = (long long)L.nd * L.DC + (long long)L.np * L.PC;
-    const long long gx = std::min<long long>((tcap + 4 * NT - 1) / (4 * NT), std::max(1, 8 * 148 / L.njobs));
+    const long long gx = std::min<long long>((tcap + 4 * NT - 1) / (4 * NT), std::max(1, 4 * 148 / L.njobs));
     dim3 grid((unsigned)std::max<long long>(1, gx), L.njobs);
     const int ps = prof_begin(2, st);
     k_attn_weights<<<grid, NT, (size_t)2 * nq * sizeof(float), st>>>(L);
