@@ -503,15 +503,16 @@ tt_status plan_attention(AttnLaunch& L, int nq, int nkv, int hd, int dense_cap, 
     L.nhg = nkv / L.HG;
     // Chunks are sized by estimated time: a token's bytes (a dense FP32 token
     // moves ~10x the bytes of a packed one), packed bytes weighted 1.4x for
-    // their lower streaming rate.  About twelve CTAs of work per SM (six waves
+    // their lower streaming rate.  About eight CTAs of work per SM (four waves
     // at two resident CTAs): the block scheduler then balances dense against
-    // packed chunks and the last partial wave is short.  Small launches (a
+    // packed chunks and the last partial wave is short (config 2: 6 / 8 / 12 /
+    // 16 CTAs of work per SM measured 598 / 544 / 585 / 588 us per step).  Small launches (a
     // sequence-sharded rank's share) keep at least 512 KB per CTA, while they
     // still fill two waves: per-CTA fixed costs stay small against the streaming.
     const double dense_tok = (double)L.HG * hd * 8.0;
     const double pbs_tok = 1.4 * ((double)L.HG * (hd / 2.0 + 2.0 * hd * 4 / 16.0 + 8.0) + 8.0);
     const double total = (double)L.njobs * L.nhg * (dense_cap * dense_tok + pbs_tok_cap * pbs_tok);
-    const double per_cta = std::max({total / (12.0 * 148.0), std::min(524288.0, total / (4.0 * 148.0)), 1.0});
+    const double per_cta = std::max({total / (8.0 * 148.0), std::min(524288.0, total / (4.0 * 148.0)), 1.0});
     auto tokens = [](double t, long long lo, long long hi) {
         long long c = ((long long)t + 31) / 32 * 32;
         return (int)std::max(lo, std::min(hi, c));

@@ -7,7 +7,7 @@
 // parallelism: per stage of NTOK positions one lane of warp 0 per position
 // issues two 1-D TMA bulk copies (its K and V rows of the group's HG kv heads,
 // one contiguous span of the token's row each) into shared memory, completion
-// counted on the stage's mbarrier; NS stages are in flight (an L2 prefetch of
+// counted on the stage's mbarrier; two stages are in flight (an L2 prefetch of
 // the stages after them measured slower: 5.1 -> 4.4 TB/s).  Every mbarrier wait is bounded (TT_ERR_TIMEOUT recorded
 // on expiry, own copies drained).  No register holds data in flight.
 //
@@ -26,7 +26,8 @@
 
 namespace tt {
 
-constexpr int kDenseNS = 3;    // stages in flight (shared memory)
+constexpr int kDenseNS = 2;    // stages in flight (shared memory; 2 leaves room for the packed
+                               // kernel's CTAs when both run at once: config 2 585 -> 562 us, against 3)
 constexpr int kDenseTPW = 4;   // positions per warp per stage
 
 // Positions per stage: TPW for every warp of the group's heads.
