@@ -24,10 +24,14 @@
 //   k_attn_merge_heads grid = (q heads, jobs, groups).  The same merge for
 //     stand-alone calls and jobs with more than 128 chunk slots (two passes
 //     above 64 slots).
-//   k_attn_weights grid = (about 8 CTAs per SM over the launch, jobs), CTAs
-//     striding over positions.  The head-mean softmax weights
-//     (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed score
-//     feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
+//   k_attn_weights grid = (one wave of CTAs over the launch, jobs), CTAs
+//     striding over positions, four per thread.  The head-mean softmax
+//     weights (fused_attn_avx2.cpp:286-300) and, for engine jobs, the decayed
+//     score feedback g[id] = decay*g[id] + w (cache_engine.cpp:511-540).
+//   k_shard_merge (sequence-sharded steps) grid = (one wave of CTAs, jobs).
+//     Every rank's rows -> output, the feedback of this rank's own tokens and
+//     the job's routing row; with the peer exchange it first waits for the
+//     other ranks' rows in its own memory.
 #include <algorithm>
 #include <climits>
 #include <mutex>

@@ -1,7 +1,7 @@
 // tt_engine.cu -- device-resident TriTierCache engine.
 //
 // Replaces TriTierCacheEngine (csrc/cache_engine.cpp).  All tier buffers and
-// counters live in HBM; one decode step is three stream-ordered launches for
+// counters live in HBM; one decode step is four stream-ordered launches for
 // any number of engines (layers / sequences):
 //   k_engine_maintain  one CTA per engine: ingest the new token into the
 //                      sink / recent-window ring, evict the oldest ring slot,
@@ -10,11 +10,16 @@
 //                      strict-argmin replace with demotion), and flush a full
 //                      waiting room into one packed block (bit-exact
 //                      quantize+pack).  cache_engine.cpp:118-269, :397-431.
-//   k_attn_partial / k_attn_merge_heads / k_attn_weights (tt_attn.cu) over
-//                      the tiers in place (no dense re-assembly,
-//                      cache_engine.cpp:433-459), with the decayed score
-//                      feedback fused into the weights pass
+//   k_attn_dense + k_attn_packed (concurrent), then k_attn_weights
+//                      (tt_attn.cu) over the tiers in place (no dense
+//                      re-assembly, cache_engine.cpp:433-459), with the
+//                      decayed score feedback fused into the weights pass
 //                      (cache_engine.cpp:511-540).
+// Sequence-sharded steps (tt_engine_step_sharded_*) run the same maintenance
+// on every rank with routing inputs from the ranks' routing rows, the
+// attention over the rank's own tokens, and k_shard_merge; the score
+// synchronisation (k_scores_pack / k_scores_unpack) runs before the steps that
+// recompute the heavy-hitter threshold.
 // The host never waits for the device inside step(); the integer state the
 // host needs for grid sizing is either deterministic (token counts) or an
 // upper bound (packed blocks).
