@@ -661,7 +661,7 @@ def ours_arm(args, cfg, rank, world, local, cores):
         "data": "synthetic",
         "config": config_dict(cfg, world, dense_l, blocks_l, step_bytes_cfg),
         "step_GBps": round(step_bytes / (ms * 1e-3) / 1e9, 1),
-        "roofline": {"kernel": "k_attn_partial (dense + packed chunks)", "bound": "hbm", "achieved": round(achieved, 1),
+        "roofline": {"kernel": "k_attn_dense + k_attn_packed (concurrent, fork to join)", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
                      "traffic": None, "bytes_per_step": part_bytes, "scratch_bytes_per_step": scratch,
                      "attention_ms_per_step": round(part_ms, 5),

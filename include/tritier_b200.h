@@ -57,7 +57,7 @@ int tt_pointer_is_device(const void* p);
  * counterpart. */
 typedef struct {
     double maintain_ms;   /* k_engine_maintain */
-    double partial_ms;    /* k_attn_partial (the dominant kernel) */
+    double partial_ms;    /* the attention kernels, dense and packed, fork to join (dominant) */
     double finalize_ms;   /* k_attn_finalize */
     int maintain_launches, partial_launches, finalize_launches;
 } tt_kernel_times;

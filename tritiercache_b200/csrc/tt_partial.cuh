@@ -3,9 +3,11 @@
 // dense kernel (tt_dense.cuh): small PTX helpers, the per-job chunk merge in
 // the last CTA.  Included by tt_attn.cu only.
 //
-// Packed chunks stream through shared memory in stages of 256 (token, kv-head)
-// pairs with 1-D TMA bulk copies (cp.async.bulk ... mbarrier::complete_tx),
-// two stages in flight.  Every mbarrier wait is bounded: on expiry the CTA
+// Head dims 64 / 128 with fp16 metadata run the tensor-core unit
+// (tt_pbs_mma.cuh: mma.sync f16, per-warp cp.async pipelines); the rest run
+// the SIMT unit described here.  Its chunks stream through shared memory in
+// stages of 256 (token, kv-head) pairs with 1-D TMA bulk copies
+// (cp.async.bulk ... mbarrier::complete_tx), two stages in flight.  Every mbarrier wait is bounded: on expiry the CTA
 // records TT_ERR_TIMEOUT in the device error word, drains its own copies
 // (again bounded) and returns.  Every copy lands in the issuing CTA's own
 // shared memory; no cluster launch.
