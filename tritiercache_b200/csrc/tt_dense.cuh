@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(NT, 2) k_attn_dense(const __grid_constant__ At
             float sv = warp_reduce_scatter<NV>(a, lane) * sc;
             if (my_t >= ntw || my_g >= G) sv = -INFINITY;
             if (my_first && sv != -INFINITY)
-                J.scores[(size_t)(kvh * G + my_g) * J.score_stride + s0 + r0 + my_t * WPH] = sv;
+                st_logit(J.scores + (size_t)(kvh * G + my_g) * J.score_stride + s0 + r0 + my_t * WPH, sv);
             float mu = sv;
 #pragma unroll
             for (int o = 1 << (SH + LOG_GM); o < 32; o <<= 1) mu = fmaxf(mu, __shfl_xor_sync(0xffffffffu, mu, o));

@@ -101,16 +101,35 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase)
         if (mbar_try_wait(bar, phase)) return true;
     return false;
 }
-// 16-byte asynchronous copy global -> shared (L2 only; cp.async groups).
+// L2 policies: the tiers stream through once (evict first), the logits the
+// attention writes are read again by the weights pass (evict last, so that
+// as many of them as fit stay in L2).
+__device__ __forceinline__ uint64_t l2_evict_first() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last() {
+    uint64_t p;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// A logit store (kept in L2 for the weights pass).
+__device__ __forceinline__ void st_logit(float* p, float v) {
+    asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(l2_evict_last()) : "memory");
+}
+// 16-byte asynchronous copy global -> shared (L2 only; cp.async groups).  No
+// eviction hint: a policy register per copy costs the tensor-core unit spills.
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
-// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar` (streaming).
 __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_addr(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
-                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
+            "r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(l2_evict_first())
+        : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -444,7 +463,7 @@ __device__ __forceinline__ void pbs_unit(const JobDesc& J, int HG, int G, int kv
         const int pos = D + s0 + tl;
 #pragma unroll
         for (int g = 0; g < GM; ++g)
-            if (g < G) J.scores[(size_t)(kvh * G + g) * J.score_stride + pos] = s[g];
+            if (g < G) st_logit(J.scores + (size_t)(kvh * G + g) * J.score_stride + pos, s[g]);
     }
     // ---- softmax, V weights ----
     float p[GM];

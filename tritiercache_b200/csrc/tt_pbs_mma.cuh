@@ -375,7 +375,7 @@ __device__ __forceinline__ void pbs_unit_mma(const JobDesc& J, int hbase, int gc
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const int t = 16 * (k >> 1) + gid + 8 * (k & 1);
-            if (k < 2 || two) srow[t] = s[k];
+            if (k < 2 || two) st_logit(srow + t, s[k]);
         }
     }
     // ---- online softmax for head tig ----
