@@ -25,9 +25,11 @@ unsharded), which every rank steps with the same inputs:
   its routing decision: the evicted token's score and the strict argmin of
   the heavy-hitter scores.
 
-A second test runs ShardedEngineStep (the Python driver of the sharded step)
-on gloo ranks with a recording stand-in for the device calls and checks its
-collective sequence.
+Two more tests run ShardedEngineStep (the Python driver of the sharded step)
+on gloo ranks with a recording stand-in for the device calls and check its
+sequence of calls and collectives: with the NCCL-style exchange (two
+all-gathers per step) and with the peer exchange (the IPC handles gathered
+once, then no collective per step but the score all-reduce).
 """
 import multiprocessing as pymp
 import socket
