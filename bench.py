@@ -1,6 +1,6 @@
 """Benchmark of the fused tiered-KV decode step on B200 (one JSON line on stdout).
 
-Headline workload (the metric's config): Llama-3-8B
+Headline workload (config 2, the configuration the metric is quoted on): Llama-3-8B
 shaped decode, 32 layers, 32 query / 8 KV heads (GQA 4:1), head_dim 128,
 context 32768, batch 1, fp16 PBS metadata, group 16.  Per layer the tiers are:
 4 sinks, the last 256 tokens in the ring, the top 5% of the middle tokens by

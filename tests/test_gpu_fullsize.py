@@ -19,7 +19,7 @@ Tolerances:
   measured drift;
 * packed words, metadata bits, ids, counters and tier membership: bit-exact.
 
-Configs (bench.CONFIGS / BASELINE configs): 1 = 32q/32kv MHA at 8k (fp16 and
+Configs (bench.CONFIGS and the benchmark's configurations): 1 = 32q/32kv MHA at 8k (fp16 and
 fp32 metadata), 2 = Llama-3-8B shape at 32k (1930 packed blocks), 5 = Qwen2-7B
 shape at 128k (28q/4kv, 7 query heads per kv head, 7766 packed blocks),
 4 = ragged batch of sequences with contexts in [2048, 65536] in one batched
