@@ -96,3 +96,31 @@ def test_no_cpu_fallback_without_cuda():
     from tritiercache_b200 import TriTierCache
     with pytest.raises(RuntimeError):
         TriTierCache(128, 32, 2, 16, 0.1)
+
+
+def test_sharded_entry_points_validate_on_the_host(libpath):
+    """The sequence-sharded calls refuse bad arguments before any device work."""
+    import ctypes as C
+    from tritiercache_b200 import _lib
+    L = _lib.lib()
+    x = C.c_void_p()
+    h = (C.c_char * 64)()
+    for world, rank in ((1, 0), (9, 0), (2, 2), (2, -1)):  # the peer exchange takes 2..8 ranks
+        assert L.tt_sharded_xch_create(world, rank, 4, 32, 128, 0, C.byref(x), h) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert b"ranks" in L.tt_last_error()
+    assert L.tt_sharded_xch_create(2, 0, 0, 32, 128, 0, C.byref(x), h) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_sharded_xch_create(2, 0, 4, 32, 128, 0, None, h) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_sharded_xch_open(None, None) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_sharded_xch_destroy(None) == 0
+    need = C.c_int(-1)
+    assert L.tt_engine_sharded_sync_needed(None, 1, C.byref(need)) == _lib.TT_ERR_INVALID_ARGUMENT
+    f = C.c_longlong(-1)
+    assert L.tt_engine_sharded_scores_floats(None, 1, C.byref(f)) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_engine_step_sharded_begin(None, 1, None, None, None, 0, 2, None, None, None) == \
+        _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_engine_step_sharded_merge(None, 1, 0, 2, None, None, None, None) == _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_engine_step_sharded_begin_xch(None, 1, None, None, None, None, 0, None) == \
+        _lib.TT_ERR_INVALID_ARGUMENT
+    assert L.tt_engine_step_sharded_merge_xch(None, 1, None, None, None) == _lib.TT_ERR_INVALID_ARGUMENT
+    # nothing to do for an empty batch
+    assert L.tt_engine_step_sharded_begin(None, 0, None, None, None, 0, 2, None, None, None) == 0
