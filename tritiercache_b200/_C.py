@@ -788,14 +788,15 @@ class ShardedEngineStep:
 _shard_steps: dict = {}
 
 
-def engine_step_batched_sharded(engines, Qs, Ks, Vs, outs, group=None) -> None:
+def engine_step_batched_sharded(engines, Qs, Ks, Vs, outs, group=None, exchange="nccl") -> None:
     """engine_step_batched over the ranks of a torch.distributed process group
     (NCCL, one process per GPU): every rank passes the same engines' handles
-    and the same inputs and receives the same outputs; each attends 1/world of
-    the tokens.  Keeps one ShardedEngineStep per (group, engine list)."""
-    key = (id(group), tuple(e._h.value for e in engines))
+    and the same inputs and receives the same outputs; each attends and scores
+    the tokens it owns.  Keeps one ShardedEngineStep per (group, engine list,
+    exchange); see ShardedEngineStep for the exchanges."""
+    key = (id(group), tuple(e._h.value for e in engines), exchange)
     s = _shard_steps.get(key)
     if s is None:
-        s = ShardedEngineStep(engines, group=group)
+        s = ShardedEngineStep(engines, group=group, exchange=exchange)
         _shard_steps[key] = s
     s(engines, Qs, Ks, Vs, outs)
