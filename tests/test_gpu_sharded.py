@@ -174,3 +174,12 @@ def test_sharded_step_argument_errors(C_):
     with pytest.raises(ValueError):
         st.merge(xa[:-1], out, rs[1:])            # routing rows not 16-byte aligned
     assert eng[0].total_processed_tokens == 300  # nothing ran
+
+
+def test_sharded_step_many_chunks(C_):
+    """One layer at 60k tokens over 2 ranks: a rank's launch has more than 128
+    chunk slots (56 dense + 117 packed), so its rows come from the separate
+    local-merge kernel instead of the attention kernels' last CTA."""
+    cfg = (32, 8, 128, 65536, 4, 256, 0.05, 0.999, 32, 16, "fp16")
+    syncs, _ = run_emulated(C_, 2, cfg, 1, steps=6, q_len=60000, seed=4242)
+    assert syncs >= 1
