@@ -3,10 +3,13 @@
 // every dense slot and every packed token exactly once, the local numbering
 // of each rank is a bijection onto what it owns, ownership follows the
 // documented rule (slot j -> rank j % w, packed granule k -> rank k % w), and
-// the ring slots' token ids are exactly [total - n2, total).  Built with nvcc
-// as a host program by tests/test_shard_map_cpu.py (no GPU needed).
+// the ring slots' token ids are exactly [total - n2, total); and the float
+// order keys behind the radix select and the routing rows' (score, slot)
+// minimum keep float order.  Built with nvcc as a host program by
+// tests/test_shard_map_cpu.py (no GPU needed).
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <vector>
 
 #include "../tritiercache_b200/csrc/tt_attn.cuh"
@@ -86,6 +89,44 @@ int main() {
         for (int p = 0; p < P; ++p)
             if (!seenp[p]) return fail("packed token not covered", w, tc, grp);
         ++cases;
+    }
+    // order keys (radix select, routing rows): key order is float order, the
+    // round trip is exact, and the complemented (score, slot) keys of the
+    // routing rows give the strict-< argmin with the first slot on ties
+    const float probes[] = {-1e30f, -2.5f, -1.0f, -1e-30f, -0.0f, 0.0f, 1e-30f, 1e-7f, 0.25f, 1.0f, 3.5f, 1e30f};
+    const int np_ = (int)(sizeof(probes) / sizeof(probes[0]));
+    for (int a = 0; a < np_; ++a) {
+        const float x = probes[a];
+        const float y = key_value(order_key(x));
+        if (memcmp(&x, &y, 4) != 0) { std::printf("FAIL key round trip %g\n", x); return 1; }
+        for (int b = 0; b < np_; ++b) {
+            const float z = probes[b];
+            if ((x < z) != (order_key(x) < order_key(z)) && !(x == 0.0f && z == 0.0f)) {
+                std::printf("FAIL key order %g %g\n", x, z);
+                return 1;
+            }
+        }
+    }
+    for (int it = 0; it < 20000; ++it) {
+        float v[4];
+        int slot[4];
+        for (int k = 0; k < 4; ++k) {
+            v[k] = (float)rnd(8) * 0.125f;  // ties are common
+            slot[k] = rnd(1000);
+        }
+        unsigned long long best = 0ull;  // complement, 0 = none
+        int bi = -1;
+        float bv = 0.f;
+        for (int k = 0; k < 4; ++k) {
+            const unsigned long long key = ~(((unsigned long long)order_key(v[k]) << 32) | (uint32_t)slot[k]);
+            best = key > best ? key : best;
+            if (bi < 0 || v[k] < bv || (v[k] == bv && slot[k] < bi)) { bv = v[k]; bi = slot[k]; }
+        }
+        const unsigned long long key = ~best;
+        if (key_value((uint32_t)(key >> 32)) != bv || (int)(uint32_t)key != bi) {
+            std::printf("FAIL routing minimum\n");
+            return 1;
+        }
     }
     std::printf("ok %d layouts\n", cases);
     return 0;

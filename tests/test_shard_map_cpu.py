@@ -7,7 +7,9 @@ positions cover every sink, heavy-hitter and ring slot and every packed token
 exactly once, that ownership follows its rule (slot j on rank j % world,
 256-token granule k on rank k % world), that each rank's packed tokens are in
 granule order, and that the ring slots' token ids are exactly
-[total - n2, total) (in logical order when unsharded).  nvcc builds it as a
+[total - n2, total) (in logical order when unsharded).  It also checks the
+float order keys (order_key / key_value) behind the threshold's radix select
+and the routing rows' complemented (score, slot) minimum.  nvcc builds it as a
 host program; no GPU is used.
 """
 import os
